@@ -1,0 +1,473 @@
+#!/usr/bin/env python3
+"""Benchmark of GLM-5.3's prefill KV-cache path on B200: fp8 KV append + paged dequant GB/s (% of HBM
+peak), tokens/s, at 1/2/4/8 GPUs by layer groups.
+
+A step is one packed prefill call (cfg3: 16 sequences, 16,384 fresh rows, prefixes from {0, 2K, 64K,
+256K}, at most 2^20 stream tokens) through the cache path of all 78 layers: per stage its row plan,
+then per layer the append (fp8 latent row + q quant, and the indexer key on indexer layers), on
+indexer layers the key gather and the top-k row plan, and the paged dequant of every sequence's
+prefix + chunk. With N GPUs the 78 layers are cut into N stages at indexer layers, one stage a GPU,
+with no collective on the data path (pipeline parallelism, as the reference deploys it).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl glmkv|reference] [--workload cfg3|cfg1|cfg2]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Rank 0 prints one JSON line. `value` is the whole job's algorithmic bytes over the slowest rank's
+device time (inputs resident in HBM); `e2e` repeats the measurement through the public API with the
+call's metadata copied in from pinned host memory and the row-plan lengths read back every step.
+`--impl reference` runs the same workload through the reference's own glue kernels (kern-glm53
+source/glm_glue.cu compiled from source, oracle/_ref) with the manifest's launch grids.
+"""
+import argparse
+import datetime
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT), str(ROOT / "kern-glm53_b200")]
+
+METRIC = "fp8 KV append+paged dequant GB/s (% HBM peak), tokens/s at 1/2/4/8 B200"
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+WORKLOADS = {
+    "cfg3": "cfg3: one 16-sequence / 16,384-row prefill call through the cache path of all 78 layers, "
+            "prefixes from {0, 2K, 64K, 256K}, stream <= 2^20 tokens, fp8 latent cache + indexer cache",
+    "cfg1": "cfg1: one 16-sequence / 16,384-row call (prefixes U[0, 32768]) through one indexer layer",
+    "cfg2": "cfg2: one 2^20-token sequence (16,384 fresh rows) through one indexer layer",
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=60)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("glmkv", "reference"), default="glmkv")
+    ap.add_argument("--workload", choices=tuple(WORKLOADS), default="cfg3")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
+    return ap.parse_args()
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+# ------------------------------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons of the given GPUs, sampled while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, ids, enabled=True):
+        self.ids, self.proc, self.lines = ids, None, []
+        self.enabled = enabled
+
+    def __enter__(self):
+        if self.enabled:
+            try:
+                cmd = ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "100"]
+                if self.ids:
+                    cmd += ["-i", ",".join(self.ids)]
+                self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except OSError:
+                self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons, pw = [], [], set(), []
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+                pw.append(float(f[3]))
+            except ValueError:
+                continue
+            for name, v in zip(self.REASONS, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(pw)}
+
+
+# ------------------------------------------------------------------------------------------ setup
+
+def device_call(torch, call, dev):
+    from glmkv.stage import CallMeta
+
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    return CallMeta(t(call.cu), t(call.seq_lens), t(call.block_table), t(call.slot_mapping), call.nseq, call.T,
+                    call.ctx)
+
+
+def fill_caches(torch, group, gen):
+    """Prefix caches of every layer: random e4m3 codes (NaN codes excluded), positive f32 tile scales,
+    N(0, 1) bf16 k_pe; indexer pages with power-of-two scales."""
+    for l, kv in group.kv.items():
+        kv.copy_(torch.randint(0, 256, kv.shape, dtype=torch.uint8, device=kv.device, generator=gen))
+        nan = (kv & 0x7F) == 0x7F
+        kv.sub_(nan.to(torch.uint8))
+        del nan
+        rows = kv.view(-1, 656)
+        sc = torch.exp2(torch.rand(rows.shape[0], 4, device=kv.device, generator=gen) * 12 - 10)
+        rows[:, 512:528] = sc.view(torch.uint8).view(-1, 16)
+        pe = torch.randn(rows.shape[0], 64, device=kv.device, generator=gen).to(torch.bfloat16)
+        rows[:, 528:] = pe.view(torch.uint8).view(-1, 128)
+    for l, idx in group.idx.items():
+        idx.copy_(torch.randint(0, 256, idx.shape, dtype=torch.uint8, device=idx.device, generator=gen))
+        pages = idx.view(-1, 64 * 132)
+        sc = torch.exp2(torch.randint(-12, 4, (pages.shape[0], 64), device=idx.device, generator=gen).float())
+        pages[:, 8192:] = sc.view(torch.uint8).view(-1, 256)
+
+
+def layer_inputs(torch, group, T, gen):
+    """Per layer: the fp8.a GEMM output [T, 2752] (N(0,1); kv_a with 1% x20 outliers) and the norm weights."""
+    from glmkv.stage import FULL, LayerInputs
+
+    dev = group.device
+    out = {}
+    for l in group.layers:
+        x = torch.randn(T, 2752, device=dev, generator=gen)
+        kv = x[:, 2048:2560]
+        kv.mul_(torch.where(torch.rand(kv.shape, device=dev, generator=gen) < 0.01, 20.0, 1.0))
+        u = lambda n: (torch.rand(n, device=dev, generator=gen) + 0.5).to(torch.bfloat16)
+        out[l] = LayerInputs(x.to(torch.bfloat16), u(2048), u(512), u(128) if l in FULL else None,
+                             (torch.randn(128, device=dev, generator=gen) * 0.1).to(torch.bfloat16) if l in FULL else None)
+        del x
+    return out
+
+
+def topk_picks(torch, call, group, gen):
+    """Per indexer layer: 2048 positions uniform in [0, klen) per row (drawn with replacement on the
+    device), or 0 .. klen - 1 then -1 when klen <= 2048."""
+    from glmkv import workload as W
+    from glmkv.stage import FULL
+
+    dev = group.device
+    klen = torch.from_numpy(W.positions(call).astype(np.int64) + 1).to(dev)
+    ar = torch.arange(2048, device=dev)
+    short = (ar[None, :] < klen[:, None]).to(torch.int32) * (ar[None, :].to(torch.int32) + 1) - 1
+    out = {}
+    for l in group.layers:
+        if l not in FULL:
+            continue
+        pick = (torch.rand(call.T, 2048, device=dev, generator=gen) * klen[:, None]).to(torch.int32)
+        out[l] = torch.where((klen <= 2048)[:, None], short, pick).contiguous()
+    return out
+
+
+# ------------------------------------------------------------------------------------------ the reference arm
+
+def run_call_reference(group, meta, inputs, ind, ctx, on_dequant=None):
+    """The same call through the reference's own kernels (oracle/_ref), manifest launch grids."""
+    from glmkv.stage import FULL
+    from oracle import ref
+
+    p = lambda t: t.data_ptr()
+    T, nseq, mp = meta.T, meta.nseq, meta.max_pages
+    ref.plan(p(meta.cu), p(meta.seq_lens), nseq, p(group.pos), p(group.ks), p(group.ke), p(group.klen),
+             p(group.row_seq), p(group.zero), T)
+    for l in group.layers:
+        a = inputs[l]
+        full = l in FULL
+        ref.mla_prep(True, p(a.x), a.x.shape[1], p(a.g_q), p(a.g_kv), p(group.rope), p(group.pos), p(meta.slot),
+                     p(group.kv[l]), p(group.idx[l]) if full else None, p(a.ik_w) if full else None,
+                     p(a.ik_b) if full else None, p(group.qq), p(group.qsf), group.sf_rows, T)
+        if full:
+            ref.idx_gather(p(group.idx[l]), p(meta.block_table), mp, p(meta.seq_lens), nseq, p(group.kg),
+                           p(group.ksf), ctx)
+            ref.topk_stream(p(ind[l]), p(group.ks), p(group.klen), p(group.tlen), T)
+        if on_dequant:
+            on_dequant(l, True)
+        ref.kv_dequant(p(group.kv[l]), p(meta.block_table), mp, p(meta.seq_lens), nseq, p(group.kvd), ctx)
+        if on_dequant:
+            on_dequant(l, False)
+
+
+# ------------------------------------------------------------------------------------------ CPU baseline
+
+def cpu_baseline(call, layers, budget_s, seed):
+    """The C oracle (a port of the reference's glue math) on the host cores: a bounded sample of the
+    same call -- layers of the workload taken in order until `budget_s` of CPU time is spent."""
+    from glmkv import traffic
+    from glmkv import workload as W
+    from glmkv.stage import FULL
+    from oracle import cpu
+
+    sys.path.insert(0, str(ROOT / "tests"))
+    from layer_case import LayerCase, run_oracle
+
+    cores = len(os.sched_getaffinity(0))
+    cpu.set_threads(cores)
+    case = LayerCase(call, "fp8", seed=seed, with_topk=True)
+    done, nbytes, elapsed = [], 0, 0.0
+    for l in layers:
+        full = l in FULL
+        h = case.host()
+        t0 = time.perf_counter()
+        run_oracle(case, h, full)
+        elapsed += time.perf_counter() - t0
+        nbytes += traffic.layer(call.T, call.ctx, full) + traffic.plan(call.T, call.nseq)
+        done.append(l)
+        if elapsed >= budget_s:
+            break
+    return {"value": nbytes / elapsed / 1e9, "unit": "GB/s", "cores": cpu.threads(), "kind": "port",
+            "sample": f"layers {done[0]}..{done[-1]} ({len(done)} of the workload's layers, same call; "
+                      f"{elapsed:.1f} s of C-oracle time, OpenMP over rows / pages)",
+            "tokens_per_s_whole_model_equiv": call.T / (elapsed / len(done) * 78)}
+
+
+# ------------------------------------------------------------------------------------------ main
+
+def main():
+    a = parse()
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != a.gpus:
+        raise SystemExit(f"--gpus {a.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    from glmkv import stage, traffic, workload as W
+
+    call = W.config(a.workload, seed=a.seed)
+    if a.workload == "cfg3":
+        first, last = stage.group_of(rank, world, T=call.T, ctx=call.ctx)
+        cuts = list(stage.cuts(world, T=call.T, ctx=call.ctx))
+    else:  # single-layer workloads: every rank runs layer 0 (an indexer layer) of its own call
+        first, last, cuts = 0, 1, [0]
+    if a.impl == "reference":
+        from oracle import ref
+        if not ref.available():
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "oracle/_ref/libglmref.so was not built (the reference tree was absent at build time)"}))
+            return
+
+    group = stage.LayerGroup(first, last, n_pages=call.n_pages, max_ctx=max(call.ctx, 1), chunk=call.T, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(1000 * a.seed + rank)
+    group.rope = torch.from_numpy(W.rope_table(int(call.seq_lens.max())).view(np.int16)).to(dev).view(torch.bfloat16)
+    fill_caches(torch, group, gen)
+    inputs = layer_inputs(torch, group, call.T, gen)
+    ind = topk_picks(torch, call, group, gen)
+    meta = device_call(torch, call, dev)
+    torch.cuda.synchronize()
+
+    if a.impl == "glmkv":
+        run = lambda hook=None: group.run_call(meta, inputs, ind, on_dequant=hook)
+    else:
+        run = lambda hook=None: run_call_reference(group, meta, inputs, ind, call.ctx, on_dequant=hook)
+    launches_per_step = group.launches_per_call()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    uuids = [str(getattr(torch.cuda.get_device_properties(dev), "uuid", ""))]
+    if world > 1:
+        allu = [None] * world
+        dist.all_gather_object(allu, uuids[0])
+        uuids = allu
+    ids = [u if u.startswith("GPU-") else f"GPU-{u}" for u in uuids if u]
+
+    # ---- device-resident timing
+    for _ in range(a.warmup):
+        run()
+    torch.cuda.synchronize()
+    barrier()
+    ev = []
+
+    def hook(l, before):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        ev.append(e)
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(ids, enabled=(rank == 0 and not a.no_clocks)) as clk:
+        torch.cuda.synchronize()
+        barrier()
+        start.record()
+        for _ in range(a.steps):
+            run(hook)
+        end.record()
+        torch.cuda.synchronize()
+        barrier()
+    ms = start.elapsed_time(end)
+    ms_max = max_over_ranks(ms)
+    dq_ms = sum(ev[i].elapsed_time(ev[i + 1]) for i in range(0, len(ev), 2))
+    dq_launches = len(ev) // 2
+
+    # ---- end to end through the public API: metadata from pinned host memory in, tlen out
+    e2e = None
+    if not a.no_e2e:
+        host = {k: getattr(meta, k).cpu().pin_memory() for k in ("cu", "seq_lens", "block_table", "slot")}
+        out = torch.empty(call.T, dtype=torch.int32).pin_memory()
+        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        d2h = out.numel() * out.element_size()
+
+        def e2e_step():
+            for k, v in host.items():
+                getattr(meta, k).copy_(v, non_blocking=True)
+            run()
+            out.copy_(group.tlen[:call.T], non_blocking=True)
+
+        for _ in range(max(1, a.warmup // 2)):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        s2.record()
+        for _ in range(a.steps):
+            e2e_step()
+        e2.record()
+        torch.cuda.synchronize()
+        wall = (time.perf_counter() - t0) * 1e3
+        barrier()
+        e2e_ms = max_over_ranks(max(s2.elapsed_time(e2), 0.0))
+        e2e = (e2e_ms, h2d, d2h, max_over_ranks(wall))
+
+    # ---- whole-job numbers
+    layer_ranges = list(zip(cuts, cuts[1:] + [stage.LAYERS if a.workload == "cfg3" else 1]))
+    total_bytes = 0
+    for f, l in (layer_ranges if a.workload == "cfg3" else [(0, 1)] * world):
+        total_bytes += traffic.plan(call.T, call.nseq) + sum(stage.layer_bytes(x, call.T, call.ctx)
+                                                             for x in range(f, l))
+    step_s = ms_max / a.steps / 1e3
+    value = total_bytes / step_s / 1e9
+    peak, peak_kind = measured_peak()
+    dq_bytes = traffic.kv_dequant(call.ctx)
+    dq_avg_s = dq_ms / max(dq_launches, 1) / 1e3
+    achieved = dq_bytes / dq_avg_s / 1e9 if dq_launches else None
+    gl = torch.tensor([launches_per_step * a.steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(gl)
+    launches_total = int(gl.item())
+
+    traffic_rec = None
+    tp = ROOT / "profiles" / "ncu_traffic.json"
+    if tp.exists():
+        try:
+            rec = json.loads(tp.read_text()).get("glm_kv_dequant")
+            if rec:
+                traffic_rec = rec["dram_bytes_per_stream_token"] * call.ctx
+        except (ValueError, KeyError):
+            traffic_rec = None
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    if a.workload == "cfg3":
+        cost = [sum(stage.layer_bytes(x, call.T, call.ctx) for x in range(f, l)) for f, l in layer_ranges]
+        ideal = sum(stage.layer_bytes(x, call.T, call.ctx) for x in range(stage.LAYERS)) / max(cost)
+    else:
+        ideal = float(world)
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": a.steps,
+        "warmup": a.warmup,
+        "ms_per_step": round(ms_max / a.steps, 4),
+        "higher_is_better": True,
+        "scaling": "strong" if a.workload == "cfg3" else "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded numpy / torch generators; no dataset or checkpoint)",
+        "impl": a.impl,
+        "config": {
+            "workload": WORKLOADS[a.workload], "seed": a.seed, "fresh_rows": call.T, "seqs": call.nseq,
+            "stream_tokens": call.ctx, "kv_cache": "fp8_ds_mla (656 B/token) + indexer 132 B/token",
+            "layers": (stage.LAYERS if a.workload == "cfg3" else world), "stage_cuts": cuts,
+            "parallelism": f"layer groups x{world} (pipeline stages at indexer layers), no collective",
+            "l2": "no flush: every layer's cache pool and stream exceed the 126 MB L2",
+            "storage": "e4m3 codes + f32 scales in, bf16 out; f32 arithmetic",
+        },
+        "tokens_per_s": round(call.T / step_s, 1),
+        "pct_hbm_peak": {"of_measured": round(value / (world * peak), 4), "of_nominal_8TBs": round(
+            value / (world * NOMINAL_HBM_GBS), 4), "measured_peak_gbs": peak, "peak_kind": peak_kind},
+        "ideal_speedup_vs_1gpu": round(ideal, 3),
+        "roofline": {"kernel": "glm_kv_dequant", "bound": "hbm", "achieved": round(achieved, 1) if achieved else None,
+                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None,
+                     "traffic": traffic_rec, "algorithmic_bytes_per_launch": dq_bytes,
+                     "avg_launch_us": round(dq_avg_s * 1e6, 2), "launches_timed": dq_launches,
+                     "peak_note": f"{peak_kind} HBM copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"},
+        "gpu_launches": launches_total,
+        "clocks": clk.summary(),
+    }
+    if e2e is not None:
+        e2e_ms, h2d, d2h, wall = e2e
+        line["e2e"] = {"value": round(total_bytes / (e2e_ms / a.steps / 1e3) / 1e9, 1), "unit": "GB/s",
+                       "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                       "ms_per_step": round(e2e_ms / a.steps, 4), "wall_ms_per_step": round(wall / a.steps, 4),
+                       "tokens_per_s": round(call.T / (e2e_ms / a.steps / 1e3), 1),
+                       "path": "glmkv LayerGroup.run_call (ctypes -> libglmkv.so) with the call's cu_seqlens, "
+                               "seq_lens, block_table, slot_mapping copied from pinned host memory each step and "
+                               "tlen read back" if a.impl == "glmkv" else
+                               "reference kernels (oracle/_ref) with the same host copies"}
+    if a.impl == "reference":
+        line["cpu_baseline"] = {"value": line["value"], "unit": "GB/s", "cores": 1, "kind": "reference",
+                                "sample": "the whole workload: the reference's glue kernels (kern-glm53 "
+                                          "source/glm_glue.cu, unmodified, compiled for sm_100a) on the GPU; the "
+                                          "reference has no CPU path"}
+    elif world == 1 and not a.no_cpu_baseline:
+        layers = list(range(first, last))
+        line["cpu_baseline"] = cpu_baseline(call, layers, a.cpu_seconds, a.seed)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

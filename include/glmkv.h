@@ -1,0 +1,115 @@
+/*
+ * glmkv: GLM-5.3's prefill KV-cache path for B200 (sm_100a), as a C ABI.
+ *
+ * Each launcher takes exactly the parameter list of the kern-glm53 manifest op it replaces, in the
+ * same order, followed by the CUDA stream to launch on. Pointers are device addresses; bf16 data is
+ * passed as `const void*` (16-bit bfloat16 elements), e4m3 as bytes. Nothing is allocated or freed;
+ * every launcher only enqueues work on `stream` and is safe to call from several host threads on
+ * different streams. The same kernels, with the same entry names and parameter lists, are also built
+ * as the cubin `glm_glue_b200.cubin` for a kern manifest.
+ *
+ * Return value: GLMKV_OK, or a GLMKV_ERR_* code when an argument is invalid (nothing is launched) or
+ * the launch failed. Device-side conditions (an invalid page number in a block table, a bounded wait
+ * that gave up) are recorded in the module's fault word, read with glmkv_fault_flags().
+ *
+ * Cache layouts (kern-glm53 source/glm_glue.cu:14-18, scripts/gen.py:53-61), slot s = page s / 64,
+ * row s % 64 of both caches:
+ *   latent cache, fp8_ds_mla: 656 B a token: 512 e4m3 (four tiles of 128) | 4 x f32 tile scales |
+ *                             64 bf16 roped k_pe; a page is 64 x 656 = 41984 B.
+ *   latent cache, bf16:       576 bf16 a token (1152 B).
+ *   indexer cache:            a page of 64 tokens is 64 x 128 e4m3 keys, then their 64 f32 scales
+ *                             (8448 B; 132 B a token).
+ */
+#ifndef GLMKV_H
+#define GLMKV_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+struct CUstream_st;
+typedef struct CUstream_st* glmkv_stream_t; /* a cudaStream_t; NULL is the legacy default stream */
+
+enum {
+  GLMKV_OK = 0,
+  GLMKV_ERR_ARG = 1,     /* a null pointer where one is required, or a size out of range */
+  GLMKV_ERR_ALIGN = 2,   /* a pointer or row stride without the alignment the kernel's accesses need */
+  GLMKV_ERR_DEVICE = 3,  /* no usable CUDA device, or the device query failed */
+  GLMKV_ERR_LAUNCH = 4   /* the kernel launch failed (cudaGetLastError after the launch) */
+};
+
+/* A row's sequence, position and indexer bounds.
+ * Replaces op `plan` -> glm_plan (kern-glm53 scripts/gen.py:95-98; source/glm_glue.cu:109-125).
+ * cu [nseq + 1] i64 prefix of the call's fresh rows, seq_lens [nseq] i32 (prefix + fresh),
+ * outputs [T]: pos, klen, row_seq, zero i32; ks, ke u32. Needs nseq >= 1, T >= 0. */
+int glmkv_plan(const int64_t* cu, const int32_t* seq_lens, int nseq, int32_t* pos, uint32_t* ks, uint32_t* ke,
+               int32_t* klen, int32_t* row_seq, int32_t* zero, int T, glmkv_stream_t stream);
+
+/* The latent-cache append with the q_a norm + quant, bf16 latent rows (--kv bf16).
+ * Replaces ops `mla_prep_full` / `mla_prep_shared` -> glm_mla_prep (kern-glm53 scripts/gen.py:172-177;
+ * source/glm_glue.cu:202-296). x [T, lda] bf16: q_a 2048 | kv_a 512 | k_pe 64 | wk 128; rope [pos][64]
+ * bf16 (32 cos | 32 sin); slot [T] i64 (< 0: no cache write); idx, ik_w, ik_b all NULL on a shared
+ * layer; qq [T, 2048] e4m3 out; qsf DeepGEMM-packed UE8M0 words [(2048 / 512)][sf_rows] out.
+ * Needs lda % 4 == 0 and lda >= 2624 (2752 with idx), x 8-byte aligned, qq and qsf 4-byte aligned,
+ * kv 16-byte aligned, sf_rows >= T. */
+int glmkv_mla_prep(const void* x, int lda, const void* g_q, const void* g_kv, const void* rope, const int32_t* pos,
+                   const int64_t* slot, void* kv, void* idx, const void* ik_w, const void* ik_b, void* qq, void* qsf,
+                   int sf_rows, int T, glmkv_stream_t stream);
+
+/* The same append into the fp8_ds_mla latent cache (the default --kv fp8).
+ * Replaces ops `mla_prep_full` / `mla_prep_shared` -> glm_mla_prep_fp8 (kern-glm53 scripts/gen.py:172-177;
+ * source/glm_glue.cu:202-287, 297-299). Same arguments and requirements as glmkv_mla_prep. */
+int glmkv_mla_prep_fp8(const void* x, int lda, const void* g_q, const void* g_kv, const void* rope,
+                       const int32_t* pos, const int64_t* slot, void* kv, void* idx, const void* ik_w, const void* ik_b,
+                       void* qq, void* qsf, int sf_rows, int T, glmkv_stream_t stream);
+
+/* The indexer keys of every sequence gathered back to back into kg [., 128] u8 and ksf [.] f32.
+ * Replaces op `idx_gather` -> glm_idx_gather (kern-glm53 scripts/gen.py:124-126;
+ * source/glm_glue.cu:357-376). block_table [nseq, max_pages] i32. Needs idx and kg 16-byte aligned. */
+int glmkv_idx_gather(const void* idx, const int32_t* block_table, int max_pages, const int32_t* seq_lens, int nseq,
+                     void* kg, float* ksf, glmkv_stream_t stream);
+
+/* The fp8 latent rows of every sequence lifted to a contiguous bf16 stream kvd [., 576].
+ * Replaces op `kv_dequant` -> glm_kv_dequant (kern-glm53 scripts/gen.py:133-135;
+ * source/glm_glue.cu:382-414). Needs kv and kvd 16-byte aligned. */
+int glmkv_kv_dequant(const void* kv, const int32_t* block_table, int max_pages, const int32_t* seq_lens, int nseq,
+                     void* kvd, glmkv_stream_t stream);
+
+/* Top-k picks [T, 2048] i32 (sequence-relative, -1 padded) -> stream rows, in place; tlen [T].
+ * Replaces op `topk_stream` -> glm_topk_stream (kern-glm53 scripts/gen.py:130-132;
+ * source/glm_glue.cu:419-428). Needs ind 16-byte aligned. */
+int glmkv_topk_stream(int32_t* ind, const uint32_t* ks, const int32_t* klen, int32_t* tlen, int T,
+                      glmkv_stream_t stream);
+
+/* Top-k picks -> cache slots through the row's page table, in place; tlen [T] (--kv bf16).
+ * Replaces op `topk_slots` -> glm_topk_slots (kern-glm53 scripts/gen.py:127-129;
+ * source/glm_glue.cu:433-444). Needs ind 16-byte aligned. */
+int glmkv_topk_slots(int32_t* ind, const int32_t* block_table, int max_pages, const int32_t* row_seq,
+                     const int32_t* klen, int32_t* tlen, int T, glmkv_stream_t stream);
+
+/* The launch shape (grid x, block x, dynamic shared memory bytes) libglmkv uses for the kernel
+ * `entry` ("glm_plan", "glm_mla_prep", "glm_mla_prep_fp8", "glm_idx_gather", "glm_kv_dequant",
+ * "glm_topk_stream", "glm_topk_slots") on the current device for a call of T fresh rows: what a kern
+ * manifest's `impl.launches` entry for the cubin must use. The persistent page kernels depend on the
+ * device's SM count only. No counterpart in the reference, whose shapes are fixed in its manifest
+ * generator (kern-glm53 scripts/gen.py:95-135, 172-177). */
+int glmkv_launch_shape(const char* entry, int T, int* grid, int* block, int* smem_bytes);
+
+/* Device-side fault bits of the current device's module (1: a bounded wait gave up; 2: a block
+ * table named a negative page, which was skipped). Synchronises the device; clears the word when
+ * `clear` is non-zero. No counterpart in the reference, whose kernels report nothing. */
+int glmkv_fault_flags(uint32_t* flags, int clear);
+
+/* A static description of an error code. */
+const char* glmkv_strerror(int code);
+
+/* ABI version of this header (major * 100 + minor). */
+int glmkv_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GLMKV_H */

@@ -1,0 +1,203 @@
+// Host side of libglmkv.so: the C ABI of include/glmkv.h. Each launcher validates its arguments on
+// the host (returning before any CUDA call when they are invalid), picks the launch shape and
+// enqueues one kernel on the caller's stream. No allocation, no synchronisation.
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "glmkv.h"
+#include "glmkv_kernels.cuh"
+
+#define GLMKV_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+using namespace glmkv;
+
+constexpr int MAX_DEVICES = 64;
+constexpr size_t DQ_SMEM = (size_t)DQ_STAGES * KV8_PAGE;
+constexpr size_t GA_SMEM = (size_t)GA_STAGES * IDX_PAGE;
+
+struct DeviceInfo {
+  int status = GLMKV_OK;
+  int sms = 0;
+  int dq_ctas = 0;  // resident dequant CTAs an SM
+  int ga_ctas = 0;  // resident gather CTAs an SM
+};
+
+std::once_flag g_once[MAX_DEVICES];
+DeviceInfo g_info[MAX_DEVICES];
+
+// Per device, once: opt the page pipelines into their shared memory, and size their persistent grids.
+const DeviceInfo* device_info() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::call_once(g_once[dev], [dev] {
+    DeviceInfo& d = g_info[dev];
+    bool ok = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess;
+    ok = ok && cudaFuncSetAttribute(glm_kv_dequant, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DQ_SMEM) ==
+                   cudaSuccess;
+    ok = ok && cudaFuncSetAttribute(glm_idx_gather, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GA_SMEM) ==
+                   cudaSuccess;
+    ok = ok && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.dq_ctas, glm_kv_dequant, DQ_THREADS, DQ_SMEM) ==
+                   cudaSuccess;
+    ok = ok && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.ga_ctas, glm_idx_gather, GA_THREADS, GA_SMEM) ==
+                   cudaSuccess;
+    if (!ok || d.sms <= 0 || d.dq_ctas <= 0 || d.ga_ctas <= 0) {
+      d.status = GLMKV_ERR_DEVICE;
+      cudaGetLastError();
+    }
+  });
+  return g_info[dev].status == GLMKV_OK ? &g_info[dev] : nullptr;
+}
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+inline int launched() { return cudaGetLastError() == cudaSuccess ? GLMKV_OK : GLMKV_ERR_LAUNCH; }
+
+template <bool FP8>
+int prep(const void* x, int lda, const void* g_q, const void* g_kv, const void* rope, const int32_t* pos,
+         const int64_t* slot, void* kv, void* idx, const void* ik_w, const void* ik_b, void* qq, void* qsf, int sf_rows,
+         int T, glmkv_stream_t stream) {
+  if (T < 0) return GLMKV_ERR_ARG;
+  if (T == 0) return GLMKV_OK;
+  if (!x || !g_q || !g_kv || !rope || !pos || !slot || !kv || !qq || !qsf) return GLMKV_ERR_ARG;
+  if (idx && (!ik_w || !ik_b)) return GLMKV_ERR_ARG;
+  if (lda < (idx ? QL + MLA + ID : QL + MLA) || sf_rows < T) return GLMKV_ERR_ARG;
+  if (lda % 4 || !aligned(x, 8) || !aligned(g_q, 8) || !aligned(g_kv, 4) || !aligned(rope, 4) || !aligned(qq, 4) ||
+      !aligned(qsf, 4) || !aligned(kv, 4) || (idx && (!aligned(idx, 4) || !aligned(ik_w, 8) || !aligned(ik_b, 8))))
+    return GLMKV_ERR_ALIGN;
+  const int rows_per_block = PREP_THREADS / 32;
+  const dim3 grid((T + rows_per_block - 1) / rows_per_block);
+  auto k = FP8 ? glm_mla_prep_fp8 : glm_mla_prep;
+  k<<<grid, PREP_THREADS, 0, (cudaStream_t)stream>>>(
+      (const bf16*)x, lda, (const bf16*)g_q, (const bf16*)g_kv, (const bf16*)rope, pos, (const long long*)slot, (u8*)kv,
+      (u8*)idx, (const bf16*)ik_w, (const bf16*)ik_b, (u8*)qq, (u8*)qsf, sf_rows, T);
+  return launched();
+}
+
+}  // namespace
+
+GLMKV_API int glmkv_plan(const int64_t* cu, const int32_t* seq_lens, int nseq, int32_t* pos, uint32_t* ks,
+                         uint32_t* ke, int32_t* klen, int32_t* row_seq, int32_t* zero, int T, glmkv_stream_t stream) {
+  if (T < 0 || nseq < 1) return GLMKV_ERR_ARG;
+  if (T == 0) return GLMKV_OK;
+  if (!cu || !seq_lens || !pos || !ks || !ke || !klen || !row_seq || !zero) return GLMKV_ERR_ARG;
+  glm_plan<<<(T + PLAN_THREADS - 1) / PLAN_THREADS, PLAN_THREADS, 0, (cudaStream_t)stream>>>(
+      (const long long*)cu, seq_lens, nseq, pos, ks, ke, klen, row_seq, zero, T);
+  return launched();
+}
+
+GLMKV_API int glmkv_mla_prep(const void* x, int lda, const void* g_q, const void* g_kv, const void* rope,
+                             const int32_t* pos, const int64_t* slot, void* kv, void* idx, const void* ik_w,
+                             const void* ik_b, void* qq, void* qsf, int sf_rows, int T, glmkv_stream_t stream) {
+  return prep<false>(x, lda, g_q, g_kv, rope, pos, slot, kv, idx, ik_w, ik_b, qq, qsf, sf_rows, T, stream);
+}
+
+GLMKV_API int glmkv_mla_prep_fp8(const void* x, int lda, const void* g_q, const void* g_kv, const void* rope,
+                                 const int32_t* pos, const int64_t* slot, void* kv, void* idx, const void* ik_w,
+                                 const void* ik_b, void* qq, void* qsf, int sf_rows, int T, glmkv_stream_t stream) {
+  return prep<true>(x, lda, g_q, g_kv, rope, pos, slot, kv, idx, ik_w, ik_b, qq, qsf, sf_rows, T, stream);
+}
+
+GLMKV_API int glmkv_idx_gather(const void* idx, const int32_t* block_table, int max_pages, const int32_t* seq_lens,
+                               int nseq, void* kg, float* ksf, glmkv_stream_t stream) {
+  if (nseq < 0 || max_pages < 0) return GLMKV_ERR_ARG;
+  if (nseq == 0) return GLMKV_OK;
+  if (!idx || !block_table || !seq_lens || !kg || !ksf) return GLMKV_ERR_ARG;
+  if (!aligned(idx, 16) || !aligned(kg, 16) || !aligned(ksf, 4)) return GLMKV_ERR_ALIGN;
+  const DeviceInfo* d = device_info();
+  if (!d) return GLMKV_ERR_DEVICE;
+  glm_idx_gather<<<d->sms * d->ga_ctas, GA_THREADS, GA_SMEM, (cudaStream_t)stream>>>(
+      (const u8*)idx, block_table, max_pages, seq_lens, nseq, (u8*)kg, ksf);
+  return launched();
+}
+
+GLMKV_API int glmkv_kv_dequant(const void* kv, const int32_t* block_table, int max_pages, const int32_t* seq_lens,
+                               int nseq, void* kvd, glmkv_stream_t stream) {
+  if (nseq < 0 || max_pages < 0) return GLMKV_ERR_ARG;
+  if (nseq == 0) return GLMKV_OK;
+  if (!kv || !block_table || !seq_lens || !kvd) return GLMKV_ERR_ARG;
+  if (!aligned(kv, 16) || !aligned(kvd, 16)) return GLMKV_ERR_ALIGN;
+  const DeviceInfo* d = device_info();
+  if (!d) return GLMKV_ERR_DEVICE;
+  glm_kv_dequant<<<d->sms * d->dq_ctas, DQ_THREADS, DQ_SMEM, (cudaStream_t)stream>>>(
+      (const u8*)kv, block_table, max_pages, seq_lens, nseq, (bf16*)kvd);
+  return launched();
+}
+
+GLMKV_API int glmkv_topk_stream(int32_t* ind, const uint32_t* ks, const int32_t* klen, int32_t* tlen, int T,
+                                glmkv_stream_t stream) {
+  if (T < 0) return GLMKV_ERR_ARG;
+  if (T == 0) return GLMKV_OK;
+  if (!ind || !ks || !klen || !tlen) return GLMKV_ERR_ARG;
+  if (!aligned(ind, 16)) return GLMKV_ERR_ALIGN;
+  glm_topk_stream<<<T, TK_THREADS, 0, (cudaStream_t)stream>>>(ind, ks, klen, tlen, T);
+  return launched();
+}
+
+GLMKV_API int glmkv_topk_slots(int32_t* ind, const int32_t* block_table, int max_pages, const int32_t* row_seq,
+                               const int32_t* klen, int32_t* tlen, int T, glmkv_stream_t stream) {
+  if (T < 0 || max_pages < 0) return GLMKV_ERR_ARG;
+  if (T == 0) return GLMKV_OK;
+  if (!ind || !block_table || !row_seq || !klen || !tlen) return GLMKV_ERR_ARG;
+  if (!aligned(ind, 16)) return GLMKV_ERR_ALIGN;
+  glm_topk_slots<<<T, TK_THREADS, 0, (cudaStream_t)stream>>>(ind, block_table, max_pages, row_seq, klen, tlen, T);
+  return launched();
+}
+
+GLMKV_API int glmkv_launch_shape(const char* entry, int T, int* grid, int* block, int* smem_bytes) {
+  if (!entry || !grid || !block || !smem_bytes || T < 0) return GLMKV_ERR_ARG;
+  const auto is = [entry](const char* s) { return strcmp(entry, s) == 0; };
+  if (is("glm_plan")) {
+    *grid = (T + PLAN_THREADS - 1) / PLAN_THREADS, *block = PLAN_THREADS, *smem_bytes = 0;
+  } else if (is("glm_mla_prep") || is("glm_mla_prep_fp8")) {
+    *grid = (T + PREP_THREADS / 32 - 1) / (PREP_THREADS / 32), *block = PREP_THREADS, *smem_bytes = 0;
+  } else if (is("glm_topk_stream") || is("glm_topk_slots")) {
+    *grid = T, *block = TK_THREADS, *smem_bytes = 0;
+  } else if (is("glm_kv_dequant") || is("glm_idx_gather")) {
+    const DeviceInfo* d = device_info();
+    if (!d) return GLMKV_ERR_DEVICE;
+    const bool dq = is("glm_kv_dequant");
+    *grid = d->sms * (dq ? d->dq_ctas : d->ga_ctas);
+    *block = dq ? DQ_THREADS : GA_THREADS;
+    *smem_bytes = (int)(dq ? DQ_SMEM : GA_SMEM);
+  } else {
+    return GLMKV_ERR_ARG;
+  }
+  return GLMKV_OK;
+}
+
+GLMKV_API int glmkv_fault_flags(uint32_t* flags, int clear) {
+  if (!flags) return GLMKV_ERR_ARG;
+  if (cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpyFromSymbol(flags, glmkv::g_fault, sizeof(uint32_t)) != cudaSuccess) {
+    cudaGetLastError();
+    return GLMKV_ERR_DEVICE;
+  }
+  if (clear) {
+    const uint32_t zero = 0;
+    if (cudaMemcpyToSymbol(glmkv::g_fault, &zero, sizeof zero) != cudaSuccess) {
+      cudaGetLastError();
+      return GLMKV_ERR_DEVICE;
+    }
+  }
+  return GLMKV_OK;
+}
+
+GLMKV_API const char* glmkv_strerror(int code) {
+  switch (code) {
+    case GLMKV_OK: return "ok";
+    case GLMKV_ERR_ARG: return "invalid argument (null pointer or size out of range)";
+    case GLMKV_ERR_ALIGN: return "misaligned pointer or row stride";
+    case GLMKV_ERR_DEVICE: return "no usable CUDA device";
+    case GLMKV_ERR_LAUNCH: return "kernel launch failed";
+    default: return "unknown glmkv error";
+  }
+}
+
+GLMKV_API int glmkv_abi_version(void) { return 100; }

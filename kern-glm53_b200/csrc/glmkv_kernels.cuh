@@ -1,0 +1,479 @@
+// The KV-cache path of GLM-5.3's prefill as sm_100a kernels. Every entry keeps the parameter list of
+// the kern-glm53 glue kernel it replaces (source/glm_glue.cu), so a manifest binds it unchanged; the
+// launch shapes (grid, block, dynamic shared memory) are this file's own and are listed with each
+// entry. Included by exactly one translation unit per module (the shared library and the cubin).
+#pragma once
+
+#include "glmkv_device.cuh"
+
+namespace glmkv {
+
+__device__ unsigned int g_fault;  // FAULT_* bits, read and cleared by the host
+
+// ================================================================================================ plan
+
+constexpr int PLAN_THREADS = 256;
+constexpr int PLAN_STAGED = 256;  // sequences whose cu / prefix a block keeps in shared memory
+
+}  // namespace glmkv
+
+// A row's sequence, position and indexer bounds (glm_glue.cu:105-125): s is the first sequence
+// with s + 1 == nseq or cu[s + 1] > r, p = seq_lens[s] - (cu[s + 1] - r), ks the u32 sum of the
+// lengths before s, ke = ks + p + 1, klen = p + 1, row_seq = s, zero = 0.
+//   grid ceil(T / 256), block 256
+extern "C" __global__ void __launch_bounds__(glmkv::PLAN_THREADS)
+    glm_plan(const long long* __restrict__ cu, const int* __restrict__ seq_lens, int nseq, int* __restrict__ pos,
+             unsigned* __restrict__ ks, unsigned* __restrict__ ke, int* __restrict__ klen, int* __restrict__ row_seq,
+             int* __restrict__ zero, int T) {
+  using namespace glmkv;
+  __shared__ long long s_cu[PLAN_STAGED + 1];
+  __shared__ unsigned s_off[PLAN_STAGED + 1];
+  __shared__ int s_len[PLAN_STAGED];
+  const int staged = nseq < PLAN_STAGED ? (nseq > 0 ? nseq : 1) : PLAN_STAGED;
+  for (int i = threadIdx.x; i < staged; i += blockDim.x) {
+    s_cu[i + 1] = cu[i + 1];
+    s_len[i] = seq_lens[i];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {  // u32 prefix of the lengths, as the reference accumulates it
+    unsigned o = 0;
+    for (int i = 0; i < staged; ++i) {
+      s_off[i] = o;
+      o += (unsigned)s_len[i];
+    }
+    s_off[staged] = o;
+  }
+  __syncthreads();
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= T) return;
+  int s = 0;
+  while (s + 1 < nseq && s + 1 < staged && s_cu[s + 1] <= r) ++s;
+  unsigned goff = s_off[s];
+  long long cnext = s_cu[s + 1];
+  int len = s_len[s];
+  if (s + 1 == staged && staged < nseq) {  // more sequences than staged: continue in global memory
+    while (s + 1 < nseq && cu[s + 1] <= r) goff += (unsigned)seq_lens[s++];
+    cnext = cu[s + 1];
+    len = seq_lens[s];
+  }
+  const int p = len - (int)(cnext - r);
+  pos[r] = p;
+  ks[r] = goff;
+  ke[r] = goff + (unsigned)p + 1u;
+  klen[r] = p + 1;
+  row_seq[r] = s;
+  zero[r] = 0;
+}
+
+// ================================================================================================ prep
+
+namespace glmkv {
+
+constexpr int PREP_THREADS = 256;  // 8 warps, one row each
+
+// One row of the latent-cache append (glm_glue.cu:196-287), run by ONE warp. Lane l holds exactly
+// the operands the reference's thread (w, l) holds for every warp w of its 256-thread block, so
+// the RMS sums are built in the reference's order (block_sum8); everything else is per element or
+// a max, which any order computes exactly.
+template <bool FP8>
+__device__ __forceinline__ void prep_row(const bf16* __restrict__ x, int lda, const bf16* __restrict__ g_q,
+                                         const bf16* __restrict__ g_kv, const bf16* __restrict__ rope,
+                                         const int* __restrict__ pos, const long long* __restrict__ slot,
+                                         u8* __restrict__ kv, u8* __restrict__ idx, const bf16* __restrict__ ik_w,
+                                         const bf16* __restrict__ ik_b, u8* __restrict__ qq, u8* __restrict__ qsf,
+                                         int sf_rows, int r, int l) {
+  const u8* row = reinterpret_cast<const u8*>(x + (size_t)r * lda);
+
+  // ---- the row's loads, all in flight at once
+  uint2 qw[16];  // q_a columns kb * 128 + 4l .. + 3
+#pragma unroll
+  for (int kb = 0; kb < 16; ++kb) qw[kb] = ld_stream_v2(row + 2 * (kb * 128 + 4 * l));
+  uint32_t kvw[8];  // kv_a columns 64w + 2l, + 1 (the reference's thread 32w + l)
+#pragma unroll
+  for (int w = 0; w < 8; ++w) kvw[w] = ld_stream_u32(row + 2 * (QL + 64 * w + 2 * l));
+  const uint32_t pew = ld_stream_u32(row + 2 * (QL + KVL + 2 * l));  // k_pe pair l
+  uint2 wkw = make_uint2(0u, 0u);
+  if (idx != nullptr) wkw = ld_stream_v2(row + 2 * (QL + KVL + 2 * HALF + 4 * l));  // wk columns 4l .. + 3
+  const long long s = slot[r];
+
+  // ---- RMS factors (glm_glue.cu:212-221): per-thread sequential partials, block_sum order
+  float part[8];
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const uint2 a = qw[2 * w], b = qw[2 * w + 1];
+    float ss = 0.f;
+    ss = __fmaf_rn(bf_lo(a.x), bf_lo(a.x), ss);
+    ss = __fmaf_rn(bf_hi(a.x), bf_hi(a.x), ss);
+    ss = __fmaf_rn(bf_lo(a.y), bf_lo(a.y), ss);
+    ss = __fmaf_rn(bf_hi(a.y), bf_hi(a.y), ss);
+    ss = __fmaf_rn(bf_lo(b.x), bf_lo(b.x), ss);
+    ss = __fmaf_rn(bf_hi(b.x), bf_hi(b.x), ss);
+    ss = __fmaf_rn(bf_lo(b.y), bf_lo(b.y), ss);
+    ss = __fmaf_rn(bf_hi(b.y), bf_hi(b.y), ss);
+    part[w] = ss;
+  }
+  const float rq = rsqrtf(block_sum8(part, l) / 2048.f + EPS);
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const float a = bf_lo(kvw[w]), b = bf_hi(kvw[w]);
+    part[w] = __fmaf_rn(a, a, __fmul_rn(b, b));  // both squares exact: round(a^2 + b^2)
+  }
+  const float rk = rsqrtf(block_sum8(part, l) / 512.f + EPS);
+
+  // ---- q_c = bf16((q_a * rq) * g_q), e4m3 per 128 columns with UE8M0 scales (glm_glue.cu:222-230)
+  uint32_t yb[16][2];
+  float am[16];
+#pragma unroll
+  for (int kb = 0; kb < 16; ++kb) {
+    const uint2 g = __ldg(reinterpret_cast<const uint2*>(g_q + kb * 128 + 4 * l));
+    const uint2 q = qw[kb];
+    const float y0 = rnd(__fmul_rn(__fmul_rn(bf_lo(q.x), rq), bf_lo(g.x)));
+    const float y1 = rnd(__fmul_rn(__fmul_rn(bf_hi(q.x), rq), bf_hi(g.x)));
+    const float y2 = rnd(__fmul_rn(__fmul_rn(bf_lo(q.y), rq), bf_lo(g.y)));
+    const float y3 = rnd(__fmul_rn(__fmul_rn(bf_hi(q.y), rq), bf_hi(g.y)));
+    am[kb] = fmaxf(fmaxf(fabsf(y0), fabsf(y1)), fmaxf(fabsf(y2), fabsf(y3)));
+    yb[kb][0] = pack_bf16x2(y0, y1);  // exact: the values are bf16 already
+    yb[kb][1] = pack_bf16x2(y2, y3);
+  }
+  unsigned e;
+  const float inv = __frcp_rn(ue8m0(max16_scatter(am, l), 1e-10f, &e));  // lane l: block kb = l >> 1
+  u8* qrow = qq + (size_t)r * QL;
+#pragma unroll
+  for (int kb = 0; kb < 16; ++kb) {
+    const float iv = __shfl_sync(FULL, inv, 2 * kb);
+    *reinterpret_cast<uint32_t*>(qrow + kb * 128 + 4 * l) =
+        fp8x4(__fmul_rn(bf_lo(yb[kb][0]), iv), __fmul_rn(bf_hi(yb[kb][0]), iv), __fmul_rn(bf_lo(yb[kb][1]), iv),
+              __fmul_rn(bf_hi(yb[kb][1]), iv));
+  }
+  // DeepGEMM's packed scales: byte (kb & 3) of word (kb >> 2, r); lane q < 4 writes word q whole.
+  unsigned word = 0;
+#pragma unroll
+  for (int m = 0; m < 4; ++m) word |= __shfl_sync(FULL, e, 2 * (4 * (l & 3) + m)) << (8 * m);
+  if (l < 4) *reinterpret_cast<unsigned*>(qsf + ((size_t)l * sf_rows + r) * 4) = word;
+
+  if (s < 0) return;  // no cache slot: nothing more to write (glm_glue.cu:231-232)
+
+  // ---- kv_norm = bf16((kv_a * rk) * g_kv) (glm_glue.cu:235)
+  const uint32_t csw = __ldg(reinterpret_cast<const unsigned*>(rope + (size_t)pos[r] * 2 * HALF) + l);
+  float k0[8], k1[8];
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const uint32_t g = __ldg(reinterpret_cast<const unsigned*>(g_kv + 64 * w + 2 * l));
+    k0[w] = rnd(__fmul_rn(__fmul_rn(bf_lo(kvw[w]), rk), bf_lo(g)));
+    k1[w] = rnd(__fmul_rn(__fmul_rn(bf_hi(kvw[w]), rk), bf_hi(g)));
+  }
+  u8* dst = kv + s * (FP8 ? KV8 : KVB);
+  if constexpr (FP8) {
+    // tiles of 128 (two virtual warps), scale amax / 448, e4m3 satfinite (glm_glue.cu:238-247)
+    float m8[8];
+#pragma unroll
+    for (int w = 0; w < 8; ++w) m8[w] = fmaxf(fabsf(k0[w]), fabsf(k1[w]));
+    const float wm = max8_scatter(m8, l);                     // lane l: warp (l >> 2) & 7
+    const float tm = fmaxf(wm, __shfl_xor_sync(FULL, wm, 4));  // lane l: tile (l >> 3) & 3
+    const float sc = __fdiv_rn(tm, 448.f);
+    const float tinv = sc > 0.f ? __frcp_rn(sc) : 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const float iv = __shfl_sync(FULL, tinv, 8 * (w >> 1));
+      *reinterpret_cast<uint16_t*>(dst + 2 * (32 * w + l)) = fp8x2(__fmul_rn(k0[w], iv), __fmul_rn(k1[w], iv));
+    }
+    const float sct = __shfl_sync(FULL, sc, 8 * (l & 3));
+    if (l < 4) reinterpret_cast<float*>(dst + KVL)[l] = sct;
+  } else {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) *reinterpret_cast<uint32_t*>(dst + 4 * (32 * w + l)) = pack_bf16x2(k0[w], k1[w]);
+  }
+
+  // ---- k_pe rope, interleaved pairs (glm_glue.cu:252-257). The bf16 x bf16 products are exact in
+  // f32, so this equals round(x1 c - x2 sn) however the reference contracted it.
+  const uint32_t ca = __shfl_sync(FULL, csw, l >> 1), cb = __shfl_sync(FULL, csw, 16 + (l >> 1));
+  {
+    const float c = (l & 1) ? bf_hi(ca) : bf_lo(ca), sn = (l & 1) ? bf_hi(cb) : bf_lo(cb);
+    const float x1 = bf_lo(pew), x2 = bf_hi(pew);
+    *reinterpret_cast<uint32_t*>(dst + (FP8 ? KVL + 16 : 2 * KVL) + 4 * l) =
+        pack_bf16x2(__fmaf_rn(x1, c, -__fmul_rn(x2, sn)), __fmaf_rn(x2, c, __fmul_rn(x1, sn)));
+  }
+
+  // ---- indexer key (glm_glue.cu:258-286): LayerNorm (eps 1e-6), rope on dims 0..63, UE8M0 e4m3
+  if (idx == nullptr) return;
+  const uint2 iw = __ldg(reinterpret_cast<const uint2*>(ik_w + 4 * l));
+  const uint2 ib = __ldg(reinterpret_cast<const uint2*>(ik_b + 4 * l));
+  const float k[4] = {bf_lo(wkw.x), bf_hi(wkw.x), bf_lo(wkw.y), bf_hi(wkw.y)};
+  const float kw[4] = {bf_lo(iw.x), bf_hi(iw.x), bf_lo(iw.y), bf_hi(iw.y)};
+  const float kbias[4] = {bf_lo(ib.x), bf_hi(ib.x), bf_lo(ib.y), bf_hi(ib.y)};
+  const float mean = warp_sum(((k[0] + k[1]) + k[2]) + k[3]) / 128.f;
+  float d[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) d[j] = __fsub_rn(k[j], mean);
+  // The f32 contractions of the reference's compiled code: d2 += d * d as one FMA a step,
+  // (d * rstd) * w + b with the last multiply fused, and the rope fusing each first product.
+  float d2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) d2 = __fmaf_rn(d[j], d[j], d2);
+  const float rstd = rsqrtf(warp_sum(d2) / 128.f + 1e-6f);
+  float n[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) n[j] = __fmaf_rn(__fmul_rn(d[j], rstd), kw[j], kbias[j]);
+  const uint32_t csh = __shfl_sync(FULL, csw, (l + 16) & 31);  // cs[32 + 2l], cs[33 + 2l]
+  if (l < 16) {
+#pragma unroll
+    for (int j = 0; j < 4; j += 2) {
+      const float c = j ? bf_hi(csw) : bf_lo(csw), sn = j ? bf_hi(csh) : bf_lo(csh), ev = n[j], od = n[j + 1];
+      n[j] = __fmaf_rn(ev, c, -__fmul_rn(od, sn));
+      n[j + 1] = __fmaf_rn(od, c, __fmul_rn(ev, sn));
+    }
+  }
+  const float amax = warp_max(fmaxf(fmaxf(fabsf(n[0]), fabsf(n[1])), fmaxf(fabsf(n[2]), fabsf(n[3]))));
+  unsigned ex;
+  const float sc = ue8m0(amax, 1e-4f, &ex);
+  u8* page = idx + (size_t)(s / PAGE) * IDX_PAGE;
+  const int i = (int)(s % PAGE);
+  *reinterpret_cast<uint32_t*>(page + i * ID + 4 * l) =
+      fp8x4(__fdiv_rn(n[0], sc), __fdiv_rn(n[1], sc), __fdiv_rn(n[2], sc), __fdiv_rn(n[3], sc));
+  if (l == 0) reinterpret_cast<float*>(page + PAGE * ID)[i] = sc;
+}
+
+}  // namespace glmkv
+
+#define GLMKV_PREP_PARAMS                                                                                       \
+  const glmkv::bf16 *__restrict__ x, int lda, const glmkv::bf16 *__restrict__ g_q,                            \
+      const glmkv::bf16 *__restrict__ g_kv, const glmkv::bf16 *__restrict__ rope, const int *__restrict__ pos,  \
+      const long long *__restrict__ slot, glmkv::u8 *__restrict__ kv, glmkv::u8 *__restrict__ idx,             \
+      const glmkv::bf16 *__restrict__ ik_w, const glmkv::bf16 *__restrict__ ik_b, glmkv::u8 *__restrict__ qq, \
+      glmkv::u8 *__restrict__ qsf, int sf_rows, int T
+#define GLMKV_PREP_ARGS x, lda, g_q, g_kv, rope, pos, slot, kv, idx, ik_w, ik_b, qq, qsf, sf_rows
+
+// `--kv bf16` append: row at kv + slot * 1152 (glm_glue.cu:294-296).
+//   grid ceil(T / 8), block 256: a warp a row
+extern "C" __global__ void __launch_bounds__(glmkv::PREP_THREADS) glm_mla_prep(GLMKV_PREP_PARAMS) {
+  const int r = blockIdx.x * (glmkv::PREP_THREADS / 32) + (threadIdx.x >> 5);
+  if (r < T) glmkv::prep_row<false>(GLMKV_PREP_ARGS, r, threadIdx.x & 31);
+}
+// fp8_ds_mla append: row at kv + slot * 656 (glm_glue.cu:297-299).
+//   grid ceil(T / 8), block 256: a warp a row
+extern "C" __global__ void __launch_bounds__(glmkv::PREP_THREADS) glm_mla_prep_fp8(GLMKV_PREP_PARAMS) {
+  const int r = blockIdx.x * (glmkv::PREP_THREADS / 32) + (threadIdx.x >> 5);
+  if (r < T) glmkv::prep_row<true>(GLMKV_PREP_ARGS, r, threadIdx.x & 31);
+}
+
+// ================================================================================================ page pipeline
+
+namespace glmkv {
+
+constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;  // a bounded wait gives up after one second
+
+struct StageMeta {
+  unsigned long long row;  // first stream row of the page
+  int n;                   // live rows in the page
+  int live;                // 0: past the last page, 1: loaded, 2: skipped (invalid page number)
+};
+
+// A persistent CTA walks the pages b, b + G, b + 2G, ... (G = gridDim.x) of the call's sequences.
+// Thread 0 keeps NSTAGE pages in flight, each one bulk copy (TMA) of the page's bytes into its
+// own shared-memory stage; all threads convert a stage once its mbarrier completes, then thread 0
+// refills it with the CTA's next page. `Op` turns a staged page into its stream rows.
+template <int NT, int NSTAGE, class Op>
+__device__ __forceinline__ void page_pipeline(const u8* __restrict__ state, const int* __restrict__ block_table,
+                                              int max_pages, const int* __restrict__ seq_lens, int nseq, const Op& op) {
+  extern __shared__ __align__(128) u8 smem[];
+  __shared__ __align__(8) unsigned long long full[NSTAGE];
+  __shared__ StageMeta meta[NSTAGE];
+  const int tid = threadIdx.x;
+  PageCursor cur;
+  unsigned pending = 0, pend_parity = 0;  // thread 0: stages with a copy in flight, and its phase
+
+  auto issue = [&](long long k) {
+    const int st = (int)(k % NSTAGE);
+    const uint32_t bar = smem_u32(&full[st]);
+    const long long g = (long long)blockIdx.x + k * (long long)gridDim.x;
+    if (!cur.seek(g)) {
+      meta[st].live = 0;
+      mbar_arrive(bar);
+      return;
+    }
+    const int j = (int)(g - cur.first);
+    const int n = min(PAGE, cur.len - j * PAGE);
+    const int phys = block_table[(size_t)cur.s * max_pages + j];
+    meta[st].row = (unsigned long long)cur.goff + (unsigned long long)j * PAGE;
+    meta[st].n = n;
+    if (phys < 0) {  // not a page of the state: skip it and flag the call
+      meta[st].live = 2;
+      atomicOr(&g_fault, FAULT_BAD_PAGE);
+      mbar_arrive(bar);
+      return;
+    }
+    meta[st].live = 1;
+    const uint32_t bytes = Op::load_bytes(n);
+    mbar_arrive_expect_tx(bar, bytes);
+    tma_load_1d(smem_u32(smem + (size_t)st * Op::STAGE), state + (size_t)phys * Op::PAGE_BYTES, bytes, bar);
+    pending |= 1u << st;
+    if ((k / NSTAGE) & 1) pend_parity |= 1u << st;
+    else pend_parity &= ~(1u << st);
+  };
+
+  if (tid == 0) {
+#pragma unroll
+    for (int st = 0; st < NSTAGE; ++st) mbar_init(smem_u32(&full[st]), 1);
+    mbar_init_fence();
+    cur.init(seq_lens, nseq);
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int k = 0; k < NSTAGE; ++k) issue(k);
+
+  for (long long k = 0;; ++k) {
+    const int st = (int)(k % NSTAGE);
+    const bool ok = mbar_wait_bounded(smem_u32(&full[st]), (uint32_t)((k / NSTAGE) & 1), WAIT_LIMIT_NS);
+    if (__syncthreads_or(!ok)) {
+      // A copy never completed: flag it, wait (bounded) for copies still in flight, and return.
+      if (tid == 0) {
+        atomicOr(&g_fault, FAULT_WAIT_TIMEOUT);
+        for (int q = 0; q < NSTAGE; ++q)
+          if (pending & (1u << q)) mbar_wait_bounded(smem_u32(&full[q]), (pend_parity >> q) & 1u, WAIT_LIMIT_NS);
+      }
+      return;
+    }
+    const StageMeta m = meta[st];
+    if (m.live == 0) break;
+    if (tid == 0) pending &= ~(1u << st);
+    if (m.live == 1) op.template consume<NT>(smem + (size_t)st * Op::STAGE, m.row, m.n, tid);
+    __syncthreads();
+    if (tid == 0) issue(k + NSTAGE);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ dequant
+
+constexpr int DQ_THREADS = 256;
+constexpr int DQ_STAGES = 4;
+
+struct DequantOp {
+  static constexpr int STAGE = KV8_PAGE;
+  static constexpr int PAGE_BYTES = KV8_PAGE;
+  bf16* kvd;
+  __device__ static uint32_t load_bytes(int n) { return (uint32_t)n * KV8; }
+
+  // Rows [0, n) of a staged page -> stream rows row0 .. row0 + n of kvd [., 576]: every e4m3 byte
+  // times its tile's f32 scale, rounded to bf16; k_pe's 128 bytes as they are (glm_glue.cu:396-413).
+  template <int NT>
+  __device__ __forceinline__ void consume(const u8* __restrict__ stg, unsigned long long row0, int n, int tid) const {
+    u8* out = reinterpret_cast<u8*>(kvd) + row0 * KVB;
+    const int nkv = n << 6;  // 16-byte output chunks of kv_norm: 64 a row
+#pragma unroll 4
+    for (int i = tid; i < nkv; i += NT) {
+      const int r = i >> 6, c = i & 63;
+      const u8* src = stg + r * KV8;
+      const uint2 q = *reinterpret_cast<const uint2*>(src + 8 * c);
+      const float sc = reinterpret_cast<const float*>(src + KVL)[c >> 4];
+      uint4 o;
+      o.x = dequant2((uint16_t)(q.x & 0xffffu), sc);
+      o.y = dequant2((uint16_t)(q.x >> 16), sc);
+      o.z = dequant2((uint16_t)(q.y & 0xffffu), sc);
+      o.w = dequant2((uint16_t)(q.y >> 16), sc);
+      *reinterpret_cast<uint4*>(out + (size_t)r * KVB + 16 * c) = o;
+    }
+    const int npe = n << 3;  // k_pe: 8 chunks a row
+    for (int i = tid; i < npe; i += NT) {
+      const int r = i >> 3, c = i & 7;
+      *reinterpret_cast<uint4*>(out + (size_t)r * KVB + 2 * KVL + 16 * c) =
+          *reinterpret_cast<const uint4*>(stg + r * KV8 + KVL + 16 + 16 * c);
+    }
+  }
+};
+
+// ------------------------------------------------------------------------------------------------ gather
+
+constexpr int GA_THREADS = 256;
+constexpr int GA_STAGES = 8;
+
+struct GatherOp {
+  static constexpr int STAGE = IDX_PAGE;
+  static constexpr int PAGE_BYTES = IDX_PAGE;
+  u8* kg;
+  float* ksf;
+  __device__ static uint32_t load_bytes(int) { return IDX_PAGE; }  // keys and scales in one copy
+
+  // Rows [0, n) of a staged index page -> kg rows row0 .. (128 bytes each) and ksf (glm_glue.cu:369-375).
+  template <int NT>
+  __device__ __forceinline__ void consume(const u8* __restrict__ stg, unsigned long long row0, int n, int tid) const {
+    uint4* dst = reinterpret_cast<uint4*>(kg + row0 * ID);
+    const uint4* src = reinterpret_cast<const uint4*>(stg);
+    const int nk = n << 3;
+#pragma unroll 2
+    for (int i = tid; i < nk; i += NT) dst[i] = src[i];
+    if (tid < n) ksf[row0 + tid] = reinterpret_cast<const float*>(stg + PAGE * ID)[tid];
+  }
+};
+
+}  // namespace glmkv
+
+// The indexer keys of every sequence back to back (glm_glue.cu:353-376): page j of sequence s lands
+// at stream rows goff(s) + 64 j, keys in kg [., 128], scales in ksf.
+//   persistent: grid = SMs x resident CTAs, block 256, dynamic smem GA_STAGES * 8448 B
+extern "C" __global__ void __launch_bounds__(glmkv::GA_THREADS)
+    glm_idx_gather(const glmkv::u8* __restrict__ idx, const int* __restrict__ block_table, int max_pages,
+                   const int* __restrict__ seq_lens, int nseq, glmkv::u8* __restrict__ kg, float* __restrict__ ksf) {
+  glmkv::page_pipeline<glmkv::GA_THREADS, glmkv::GA_STAGES>(idx, block_table, max_pages, seq_lens, nseq,
+                                                            glmkv::GatherOp{kg, ksf});
+}
+
+// The fp8 latent rows of every sequence lifted to bf16 back to back, the stream of glm_idx_gather
+// (glm_glue.cu:378-414).
+//   persistent: grid = SMs x resident CTAs, block 256, dynamic smem DQ_STAGES * 41984 B
+extern "C" __global__ void __launch_bounds__(glmkv::DQ_THREADS, 1)
+    glm_kv_dequant(const glmkv::u8* __restrict__ kv, const int* __restrict__ block_table, int max_pages,
+                   const int* __restrict__ seq_lens, int nseq, glmkv::bf16* __restrict__ kvd) {
+  glmkv::page_pipeline<glmkv::DQ_THREADS, glmkv::DQ_STAGES>(kv, block_table, max_pages, seq_lens, nseq,
+                                                            glmkv::DequantOp{kvd});
+}
+
+// ================================================================================================ row plans
+
+namespace glmkv {
+constexpr int TK_THREADS = 256;  // a row of 2048 indices: two int4 a thread
+
+__device__ __forceinline__ int stream_row(int k, unsigned base) { return k < 0 ? -1 : (int)(base + (unsigned)k); }
+__device__ __forceinline__ int slot_of(int k, const int* __restrict__ bt) {
+  return k < 0 ? -1 : bt[k >> 6] * PAGE + (k & (PAGE - 1));
+}
+}  // namespace glmkv
+
+// Sequence-relative top-k picks (-1 past a short row's keys) -> rows of the dequantized stream, in
+// place; tlen = min(klen, 2048) (glm_glue.cu:416-428).
+//   grid T, block 256
+extern "C" __global__ void __launch_bounds__(glmkv::TK_THREADS)
+    glm_topk_stream(int* __restrict__ ind, const unsigned* __restrict__ ks, const int* __restrict__ klen,
+                    int* __restrict__ tlen, int T) {
+  using namespace glmkv;
+  const int r = blockIdx.x;
+  int4* row = reinterpret_cast<int4*>(ind + (size_t)r * TOPK);
+  const unsigned base = ks[r];
+  for (int i = threadIdx.x; i < TOPK / 8; i += blockDim.x) {
+    int4 a = row[i], b = row[i + TOPK / 8];
+    a = make_int4(stream_row(a.x, base), stream_row(a.y, base), stream_row(a.z, base), stream_row(a.w, base));
+    b = make_int4(stream_row(b.x, base), stream_row(b.y, base), stream_row(b.z, base), stream_row(b.w, base));
+    row[i] = a;
+    row[i + TOPK / 8] = b;
+  }
+  if (threadIdx.x == 0) tlen[r] = min(klen[r], TOPK);
+}
+
+// Sequence-relative top-k picks -> cache slots through the row's page table, in place; tlen as
+// above (glm_glue.cu:430-444).
+//   grid T, block 256
+extern "C" __global__ void __launch_bounds__(glmkv::TK_THREADS)
+    glm_topk_slots(int* __restrict__ ind, const int* __restrict__ block_table, int max_pages,
+                   const int* __restrict__ row_seq, const int* __restrict__ klen, int* __restrict__ tlen, int T) {
+  using namespace glmkv;
+  const int r = blockIdx.x;
+  const int* bt = block_table + (size_t)row_seq[r] * max_pages;
+  int4* row = reinterpret_cast<int4*>(ind + (size_t)r * TOPK);
+  for (int i = threadIdx.x; i < TOPK / 8; i += blockDim.x) {
+    int4 a = row[i], b = row[i + TOPK / 8];
+    a = make_int4(slot_of(a.x, bt), slot_of(a.y, bt), slot_of(a.z, bt), slot_of(a.w, bt));
+    b = make_int4(slot_of(b.x, bt), slot_of(b.y, bt), slot_of(b.z, bt), slot_of(b.w, bt));
+    row[i] = a;
+    row[i + TOPK / 8] = b;
+  }
+  if (threadIdx.x == 0) tlen[r] = min(klen[r], TOPK);
+}

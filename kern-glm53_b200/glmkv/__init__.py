@@ -1,0 +1,12 @@
+"""glmkv: GLM-5.3's prefill KV-cache path on B200 (sm_100a).
+
+Drop-in replacement for the cache ops of kern-glm53's ``source/glm_glue.cu`` (plan, the fp8 / bf16
+latent-cache append with the indexer-key append, the indexer-key gather, the paged fp8 -> bf16
+dequant, the top-k row plans). The kernels are CUDA in ``libglmkv.so`` (C ABI: ``include/glmkv.h``);
+this package binds them with ctypes and uses PyTorch only to own device memory.
+"""
+from ._lib import CUBIN_PATH, LIB_PATH, GlmKvError, fault_flags, launch_shape, lib, strerror
+from .ops import (idx_gather, kv_dequant, mla_prep_full, mla_prep_shared, plan, topk_slots, topk_stream)
+
+__all__ = ["CUBIN_PATH", "LIB_PATH", "GlmKvError", "fault_flags", "launch_shape", "lib", "strerror", "plan", "mla_prep_full",
+           "mla_prep_shared", "idx_gather", "kv_dequant", "topk_stream", "topk_slots"]

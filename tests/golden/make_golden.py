@@ -1,0 +1,126 @@
+"""Golden vectors of the REFERENCE glue kernels, to pin the C oracle on machines without a GPU.
+
+Runs kern-glm53 ``source/glm_glue.cu`` (compiled from source for sm_100a into ``oracle/_ref``) on
+seeded inputs from ``glmkv.workload`` and stores its outputs under ``tests/golden/``:
+
+* ``ref_small_<case>.npz``: one layer of a small call -- every output, with the caches reduced to the
+  rows this call wrote (the rest of each pool is the seeded input);
+* ``ref_digests.json``: for larger calls, SHA-256 of each output that does not depend on rsqrtf
+  (plan, row plan, and the prefix rows of the gathered / dequantized streams), and of the inputs, so a
+  CPU run can tell generator drift from an oracle mismatch.
+
+Needs a CUDA device and ``oracle/_ref/libglmref.so``:
+
+    python tests/golden/make_golden.py [--out tests/golden]
+"""
+import argparse
+import hashlib
+import json
+import pathlib
+import sys
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+sys.path[:0] = [str(ROOT), str(ROOT / "kern-glm53_b200"), str(ROOT / "tests")]
+
+from glmkv import workload as W  # noqa: E402
+from layer_case import LayerCase, run_reference, to_host  # noqa: E402
+
+# (name, call config, call seed, case seed, kv dtype, full layer, zero tiles)
+SMALL = [
+    ("fp8_full", "small", 21, 22, "fp8", True, 2),
+    ("fp8_shared", "small", 21, 23, "fp8", False, 0),
+    ("bf16_full", "small", 24, 25, "bf16", True, 2),
+]
+DIGEST = [
+    ("cfg0_fp8_full", "cfg0", 3, 11, "fp8", True, 0),
+    ("cfg4_fp8_full", "cfg4", 3, 11, "fp8", True, 4),
+    ("cfg4_bf16_full", "cfg4", 3, 11, "bf16", True, 4),
+    ("cfg1_fp8_full", "cfg1", 3, 11, "fp8", True, 16),
+]
+EXACT = ("pos", "ks", "ke", "klen", "row_seq", "zero", "ind", "tlen")
+
+
+def small_call(seed):
+    """Three short sequences: a prefix with a ragged fresh chunk, an empty prefix, a one-token chunk."""
+    rng = np.random.default_rng(seed)
+    return W.make_call([100, 0, 129], [40, 23, 1], rng, max_pages=8, spare_pages=3, name="small", seed=seed)
+
+
+def call_of(cfg, seed):
+    return small_call(seed) if cfg == "small" else W.config(cfg, seed=seed)
+
+
+def sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def input_digest(case):
+    h = hashlib.sha256()
+    for a in (case.x, case.rope, case.w.g_q, case.w.g_kv, case.w.ik_w, case.w.ik_b, case.kv_pool, case.idx_pool,
+              case.call.block_table, case.call.slot_mapping, case.call.seq_lens, case.call.cu):
+        h.update(np.ascontiguousarray(a).tobytes())
+    if case.ind is not None:
+        h.update(case.ind.tobytes())
+    return h.hexdigest()
+
+
+def prefix_rows(call):
+    """Stream rows that hold prefix tokens (written before this call, so independent of its append)."""
+    goff = np.concatenate([[0], np.cumsum(call.seq_lens.astype(np.int64))[:-1]])
+    return np.concatenate([g + np.arange(p, dtype=np.int64) for g, p in zip(goff, call.prefix)])
+
+
+def fresh_cache_rows(case, res):
+    """The cache rows this call wrote: latent rows and indexer (keys, scale) at its slots."""
+    slots = case.call.slot_mapping
+    row = 656 if case.kv_dtype == "fp8" else 1152
+    kv = res["kv"].reshape(-1, row)[slots]
+    pages = res["idx"].reshape(-1, 64 * 132)
+    keys = np.stack([pages[s // 64, (s % 64) * 128:(s % 64) * 128 + 128] for s in slots])
+    scs = np.stack([pages[s // 64, 8192 + 4 * (s % 64):8196 + 4 * (s % 64)] for s in slots])
+    return kv, keys, scs
+
+
+def run_case(torch, spec):
+    name, cfg, cseed, seed, kv_dtype, full, zt = spec
+    case = LayerCase(call_of(cfg, cseed), kv_dtype=kv_dtype, seed=seed, zero_tiles=zt)
+    d = case.device(torch, torch.device("cuda:0"))
+    run_reference(case, d, full)
+    torch.cuda.synchronize()
+    return case, to_host(d, torch)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", default=str(HERE))
+    a = ap.parse_args()
+    out = pathlib.Path(a.out)
+    out.mkdir(parents=True, exist_ok=True)
+    import torch
+
+    for spec in SMALL:
+        case, res = run_case(torch, spec)
+        kv, keys, scs = fresh_cache_rows(case, res)
+        keep = {k: v for k, v in res.items() if k not in ("kv", "idx")}
+        np.savez_compressed(out / f"ref_small_{spec[0]}.npz", input_sha=np.array(input_digest(case)), kv_fresh=kv,
+                            idx_keys_fresh=keys, idx_sc_fresh=scs, **keep)
+    digests = {}
+    for spec in DIGEST:
+        case, res = run_case(torch, spec)
+        pr = prefix_rows(case.call)
+        dg = {"input_sha": input_digest(case), **{k: sha(res[k]) for k in EXACT if k in res}}
+        if case.kv_dtype == "fp8":
+            dg["kvd_prefix"] = sha(res["kvd"].reshape(-1, 576)[pr])
+        if spec[5]:
+            dg["kg_prefix"] = sha(res["kg"].reshape(-1, 128)[pr])
+            dg["ksf_prefix"] = sha(res["ksf"][pr])
+        digests[spec[0]] = dg
+    (out / "ref_digests.json").write_text(json.dumps(digests, indent=1, sort_keys=True) + "\n")
+    print("golden vectors written to", out)
+
+
+if __name__ == "__main__":
+    main()

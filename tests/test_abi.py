@@ -1,0 +1,70 @@
+"""The C ABI without a GPU: the library loads, exports every symbol include/glmkv.h declares, and
+rejects invalid arguments on the host (before any CUDA call)."""
+import ctypes
+import pathlib
+import re
+
+import pytest
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "glmkv.h"
+
+
+def declared():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return re.findall(r"^(?:int|const char\*)\s+(glmkv_\w+)\s*\(", text, flags=re.M)
+
+
+def test_header_declares_the_manifest_ops():
+    names = set(declared())
+    assert {"glmkv_plan", "glmkv_mla_prep", "glmkv_mla_prep_fp8", "glmkv_idx_gather", "glmkv_kv_dequant",
+            "glmkv_topk_stream", "glmkv_topk_slots"} <= names
+
+
+def test_library_exports_every_declared_symbol(built_lib):
+    lib = ctypes.CDLL(str(built_lib))
+    for name in declared():
+        assert hasattr(lib, name), name
+    import glmkv
+    assert set(declared()) == set(glmkv._lib.SIGNATURES)
+    assert glmkv.lib().glmkv_abi_version() == 100
+
+
+def test_host_side_argument_checks(built_lib):
+    import glmkv
+    from glmkv import _lib
+
+    L = glmkv.lib()
+    A = 0x10000  # an aligned, never dereferenced address: every call below returns before any CUDA call
+    assert L.glmkv_plan(A, A, 0, A, A, A, A, A, A, 16, None) == _lib.ERR_ARG          # nseq < 1
+    assert L.glmkv_plan(A, A, 1, A, A, A, A, A, A, -1, None) == _lib.ERR_ARG          # T < 0
+    assert L.glmkv_plan(A, A, 1, None, A, A, A, A, A, 16, None) == _lib.ERR_ARG       # null output
+    assert L.glmkv_plan(A, A, 1, A, A, A, A, A, A, 0, None) == _lib.OK                # T = 0: nothing to do
+    args = [A, 2752, A, A, A, A, A, A, A, A, A, A, A, 64, 64, None]
+    for fn in (L.glmkv_mla_prep, L.glmkv_mla_prep_fp8):
+        bad = list(args); bad[1] = 2748 - 64
+        assert fn(*bad) == _lib.ERR_ARG                                                 # lda too small
+        bad = list(args); bad[1] = 2754
+        assert fn(*bad) == _lib.ERR_ALIGN                                               # lda % 4
+        bad = list(args); bad[0] = A + 2
+        assert fn(*bad) == _lib.ERR_ALIGN                                               # x not 8-aligned
+        bad = list(args); bad[9] = None
+        assert fn(*bad) == _lib.ERR_ARG                                                 # idx without ik_w
+        bad = list(args); bad[13] = 32
+        assert fn(*bad) == _lib.ERR_ARG                                                 # sf_rows < T
+        bad = list(args); bad[14] = 0
+        assert fn(*bad) == _lib.OK                                                      # T = 0
+        shared = list(args); shared[1] = 2624; shared[8] = shared[9] = shared[10] = None; shared[14] = -1
+        assert fn(*shared) == _lib.ERR_ARG                                              # T < 0
+    assert L.glmkv_kv_dequant(A + 8, A, 16, A, 1, A, None) == _lib.ERR_ALIGN
+    assert L.glmkv_kv_dequant(A, A, 16, A, 1, A + 8, None) == _lib.ERR_ALIGN
+    assert L.glmkv_kv_dequant(A, A, 16, A, -1, A, None) == _lib.ERR_ARG
+    assert L.glmkv_kv_dequant(A, A, 16, A, 0, A, None) == _lib.OK
+    assert L.glmkv_idx_gather(A, A, 16, A, 1, A + 4, A, None) == _lib.ERR_ALIGN
+    assert L.glmkv_idx_gather(A, A, -1, A, 1, A, A, None) == _lib.ERR_ARG
+    assert L.glmkv_topk_stream(A + 4, A, A, A, 8, None) == _lib.ERR_ALIGN
+    assert L.glmkv_topk_slots(A, A, 16, A, A, None, 8, None) == _lib.ERR_ARG
+    with pytest.raises(glmkv.GlmKvError):
+        _lib.call("glmkv_topk_stream", A + 4, A, A, A, 8, None)
+    assert "misaligned" in glmkv.strerror(_lib.ERR_ALIGN)
