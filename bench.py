@@ -19,7 +19,6 @@ call's metadata copied in from pinned host memory and the row-plan lengths read 
 source/glm_glue.cu compiled from source, oracle/_ref) with the manifest's launch grids.
 """
 import argparse
-import datetime
 import json
 import os
 import pathlib
@@ -257,19 +256,15 @@ def cpu_baseline(call, layers, budget_s, seed):
 def main():
     a = parse()
     import torch
-    import torch.distributed as dist
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    from glmkv import dist as gd, stage, traffic, workload as W
+
+    world, rank, local = gd.env()
     if world != a.gpus:
         raise SystemExit(f"--gpus {a.gpus} but WORLD_SIZE {world}")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-
-    from glmkv import stage, traffic, workload as W
+    gd.init("nccl", timeout_s=300, device=dev)
 
     call = W.config(a.workload, seed=a.seed)
     if a.workload == "cfg3":
@@ -300,22 +295,9 @@ def main():
         run = lambda hook=None: run_call_reference(group, meta, inputs, ind, call.ctx, on_dequant=hook)
     launches_per_step = group.launches_per_call()
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    uuids = [str(getattr(torch.cuda.get_device_properties(dev), "uuid", ""))]
-    if world > 1:
-        allu = [None] * world
-        dist.all_gather_object(allu, uuids[0])
-        uuids = allu
+    barrier = gd.barrier
+    max_over_ranks = lambda v: gd.max_over_ranks(v, device=dev)
+    uuids = gd.gather_objects(str(getattr(torch.cuda.get_device_properties(dev), "uuid", "")))
     ids = [u if u.startswith("GPU-") else f"GPU-{u}" for u in uuids if u]
 
     # ---- device-resident timing
@@ -387,10 +369,7 @@ def main():
     dq_bytes = traffic.kv_dequant(call.ctx)
     dq_avg_s = dq_ms / max(dq_launches, 1) / 1e3
     achieved = dq_bytes / dq_avg_s / 1e9 if dq_launches else None
-    gl = torch.tensor([launches_per_step * a.steps], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(gl)
-    launches_total = int(gl.item())
+    launches_total = int(gd.sum_over_ranks(launches_per_step * a.steps, device=dev))
 
     traffic_rec = None
     tp = ROOT / "profiles" / "ncu_traffic.json"
@@ -403,8 +382,7 @@ def main():
             traffic_rec = None
 
     if rank != 0:
-        if world > 1:
-            dist.destroy_process_group()
+        gd.finish()
         return
 
     if a.workload == "cfg3":
@@ -465,8 +443,7 @@ def main():
         layers = list(range(first, last))
         line["cpu_baseline"] = cpu_baseline(call, layers, a.cpu_seconds, a.seed)
     print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    gd.finish()
 
 
 if __name__ == "__main__":

@@ -35,9 +35,6 @@ def _run_both(case, cuda, full=True):
     return to_host(d_mine, torch), (to_host(d_ref, torch) if _ref_available() else None)
 
 
-EXACT = ("pos", "ks", "ke", "klen", "row_seq", "zero", "kg", "ksf", "kvd", "ind", "tlen")
-
-
 def _assert_all_equal(got, want, what):
     for k in got:
         g, w = got[k], want[k]
@@ -68,20 +65,22 @@ def test_layer_vs_reference_and_oracle(cuda, name, kv_dtype, full, zero_tiles):
         _assert_all_equal(got, ref, f"{name}/{kv_dtype}/{'full' if full else 'shared'} vs reference")
     h = case.host()
     run_oracle(case, h, full)
-    want = to_host_oracle(h)
-    for k in EXACT:
-        if k in got and k in want and want[k] is not None:
-            g, w = got[k], want[k]
-            if k == "ksf":
-                g, w = g.view(np.uint32), w.view(np.uint32)
-            if not full and k in ("kg", "ksf", "ind", "tlen"):
-                continue
-            assert_equal(g, w, f"{name} vs oracle: {k}")
-    assert_prep_close(got, want, case, full, what=f"{name} vs oracle")
-
-
-def to_host_oracle(h):
-    return {k: v for k, v in h.items() if k not in ("x", "rope", "cu", "seq_lens", "block_table", "slot")}
+    for k in ("pos", "ks", "ke", "klen", "row_seq", "zero") + (("ind", "tlen") if full else ()):
+        assert_equal(got[k], h[k], f"{name} vs oracle: {k}")
+    # the append: within the rsqrtf tolerance of the oracle
+    assert_prep_close(got, h, case, full, what=f"{name} vs oracle")
+    # gather and dequant of the device's own cache state (fresh rows included): bit-exact
+    from oracle import cpu
+    c = case.call
+    if full:
+        kg, ksf = np.zeros_like(h["kg"]), np.zeros_like(h["ksf"])
+        cpu.idx_gather(got["idx"], c.block_table, c.max_pages, c.seq_lens, c.nseq, kg, ksf)
+        assert_equal(got["kg"], kg, f"{name} vs oracle: kg")
+        assert_equal(got["ksf"].view(np.uint32), ksf.view(np.uint32), f"{name} vs oracle: ksf")
+    if kv_dtype == "fp8":
+        kvd = np.zeros_like(h["kvd"])
+        cpu.kv_dequant(got["kv"], c.block_table, c.max_pages, c.seq_lens, c.nseq, kvd)
+        assert_equal(got["kvd"], kvd, f"{name} vs oracle: kvd")
 
 
 @needs_ref
