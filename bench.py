@@ -235,20 +235,21 @@ def cpu_baseline(call, layers, budget_s, seed):
     cpu.set_threads(cores)
     case = LayerCase(call, "fp8", seed=seed, with_topk=True)
     done, nbytes, elapsed = [], 0, 0.0
-    for l in layers:
-        full = l in FULL
-        h = case.host()
-        t0 = time.perf_counter()
-        run_oracle(case, h, full)
-        elapsed += time.perf_counter() - t0
-        nbytes += traffic.layer(call.T, call.ctx, full) + traffic.plan(call.T, call.nseq)
-        done.append(l)
-        if elapsed >= budget_s:
-            break
+    h = case.host()
+    while elapsed < budget_s:  # the layers in order, again from the first while budget is left
+        for l in layers:
+            full = l in FULL
+            t0 = time.perf_counter()
+            run_oracle(case, h, full)
+            elapsed += time.perf_counter() - t0
+            nbytes += traffic.layer(call.T, call.ctx, full) + traffic.plan(call.T, call.nseq)
+            done.append(l)
+            if elapsed >= budget_s:
+                break
     return {"value": nbytes / elapsed / 1e9, "unit": "GB/s", "cores": cpu.threads(), "kind": "port",
-            "sample": f"layers {done[0]}..{done[-1]} ({len(done)} of the workload's layers, same call; "
-                      f"{elapsed:.1f} s of C-oracle time, OpenMP over rows / pages)",
-            "tokens_per_s_whole_model_equiv": call.T / (elapsed / len(done) * 78)}
+            "sample": f"{len(done)} layer passes of the workload's layers in order (same call, one layer's "
+                      f"cache state reused), {elapsed:.1f} s of C-oracle time, OpenMP over rows / pages",
+            "tokens_per_s": call.T / (elapsed / len(done) * len(layers))}
 
 
 # ------------------------------------------------------------------------------------------ main
@@ -305,12 +306,19 @@ def main():
         run()
     torch.cuda.synchronize()
     barrier()
-    ev = []
+    # per-kernel timing inside the timed region: one dequant launch a step (a different layer each
+    # step), bracketed by two events on the launch stream
+    ev, step_no = [], [0]
+    layers = group.layers
 
     def hook(l, before):
+        if l != layers[step_no[0] % len(layers)]:
+            return
         e = torch.cuda.Event(enable_timing=True)
         e.record()
         ev.append(e)
+        if not before:
+            step_no[0] += 1
 
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(ids, enabled=(rank == 0 and not a.no_clocks)) as clk:

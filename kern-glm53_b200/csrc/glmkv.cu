@@ -3,6 +3,7 @@
 // enqueues one kernel on the caller's stream. No allocation, no synchronisation.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 
@@ -22,8 +23,9 @@ constexpr size_t GA_SMEM = (size_t)GA_STAGES * IDX_PAGE;
 struct DeviceInfo {
   int status = GLMKV_OK;
   int sms = 0;
-  int dq_ctas = 0;  // resident dequant CTAs an SM
-  int ga_ctas = 0;  // resident gather CTAs an SM
+  int dq_ctas = 0;    // resident dequant CTAs an SM
+  int ga_ctas = 0;    // resident gather CTAs an SM
+  int prep_ctas = 0;  // resident append CTAs an SM
 };
 
 std::once_flag g_once[MAX_DEVICES];
@@ -47,7 +49,11 @@ const DeviceInfo* device_info() {
                    cudaSuccess;
     ok = ok && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.ga_ctas, glm_idx_gather, GA_THREADS, GA_SMEM) ==
                    cudaSuccess;
-    if (!ok || d.sms <= 0 || d.dq_ctas <= 0 || d.ga_ctas <= 0) {
+    for (auto k : {glm_mla_prep, glm_mla_prep_fp8})
+      ok = ok && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM) == cudaSuccess;
+    ok = ok && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.prep_ctas, glm_mla_prep_fp8, PREP_THREADS,
+                                                             PREP_SMEM) == cudaSuccess;
+    if (!ok || d.sms <= 0 || d.dq_ctas <= 0 || d.ga_ctas <= 0 || d.prep_ctas <= 0) {
       d.status = GLMKV_ERR_DEVICE;
       cudaGetLastError();
     }
@@ -71,10 +77,11 @@ int prep(const void* x, int lda, const void* g_q, const void* g_kv, const void* 
   if (lda % 4 || !aligned(x, 8) || !aligned(g_q, 8) || !aligned(g_kv, 4) || !aligned(rope, 4) || !aligned(qq, 4) ||
       !aligned(qsf, 4) || !aligned(kv, 4) || (idx && (!aligned(idx, 4) || !aligned(ik_w, 8) || !aligned(ik_b, 8))))
     return GLMKV_ERR_ALIGN;
-  const int rows_per_block = PREP_THREADS / 32;
-  const dim3 grid((T + rows_per_block - 1) / rows_per_block);
+  const DeviceInfo* d = device_info();
+  if (!d) return GLMKV_ERR_DEVICE;
+  const int grid = std::min(d->sms * d->prep_ctas, (T + PREP_WARPS - 1) / PREP_WARPS);
   auto k = FP8 ? glm_mla_prep_fp8 : glm_mla_prep;
-  k<<<grid, PREP_THREADS, 0, (cudaStream_t)stream>>>(
+  k<<<grid, PREP_THREADS, PREP_SMEM, (cudaStream_t)stream>>>(
       (const bf16*)x, lda, (const bf16*)g_q, (const bf16*)g_kv, (const bf16*)rope, pos, (const long long*)slot, (u8*)kv,
       (u8*)idx, (const bf16*)ik_w, (const bf16*)ik_b, (u8*)qq, (u8*)qsf, sf_rows, T);
   return launched();
@@ -155,17 +162,19 @@ GLMKV_API int glmkv_launch_shape(const char* entry, int T, int* grid, int* block
   const auto is = [entry](const char* s) { return strcmp(entry, s) == 0; };
   if (is("glm_plan")) {
     *grid = (T + PLAN_THREADS - 1) / PLAN_THREADS, *block = PLAN_THREADS, *smem_bytes = 0;
-  } else if (is("glm_mla_prep") || is("glm_mla_prep_fp8")) {
-    *grid = (T + PREP_THREADS / 32 - 1) / (PREP_THREADS / 32), *block = PREP_THREADS, *smem_bytes = 0;
   } else if (is("glm_topk_stream") || is("glm_topk_slots")) {
     *grid = T, *block = TK_THREADS, *smem_bytes = 0;
-  } else if (is("glm_kv_dequant") || is("glm_idx_gather")) {
+  } else if (is("glm_kv_dequant") || is("glm_idx_gather") || is("glm_mla_prep") || is("glm_mla_prep_fp8")) {
     const DeviceInfo* d = device_info();
     if (!d) return GLMKV_ERR_DEVICE;
-    const bool dq = is("glm_kv_dequant");
-    *grid = d->sms * (dq ? d->dq_ctas : d->ga_ctas);
-    *block = dq ? DQ_THREADS : GA_THREADS;
-    *smem_bytes = (int)(dq ? DQ_SMEM : GA_SMEM);
+    if (is("glm_kv_dequant")) {
+      *grid = d->sms * d->dq_ctas, *block = DQ_THREADS, *smem_bytes = (int)DQ_SMEM;
+    } else if (is("glm_idx_gather")) {
+      *grid = d->sms * d->ga_ctas, *block = GA_THREADS, *smem_bytes = (int)GA_SMEM;
+    } else {
+      *grid = std::min(d->sms * d->prep_ctas, (T + PREP_WARPS - 1) / PREP_WARPS);
+      *block = PREP_THREADS, *smem_bytes = PREP_SMEM;
+    }
   } else {
     return GLMKV_ERR_ARG;
   }

@@ -9,6 +9,7 @@
 namespace glmkv {
 
 __device__ unsigned int g_fault;  // FAULT_* bits, read and cleared by the host
+constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;  // a bounded wait gives up after one second
 
 // ================================================================================================ plan
 
@@ -69,71 +70,118 @@ extern "C" __global__ void __launch_bounds__(glmkv::PLAN_THREADS)
 
 namespace glmkv {
 
-constexpr int PREP_THREADS = 256;  // 8 warps, one row each
+constexpr int PREP_WARPS = 8;                            // a CTA: 8 warps, each its own rows
+constexpr int PREP_THREADS = 32 * PREP_WARPS;
+constexpr int PREP_BUFS = 2;                             // rows a warp holds in shared memory
+constexpr int PREP_ROW = 2 * (QL + KVL + 2 * HALF + ID); // 5504 B: one [q_a | kv_a | k_pe | wk] row
+constexpr int PREP_WGT = 4 * (QL + KVL + 2 * ID);        // f32 g_q | g_kv | ik_w | ik_b
+constexpr int PREP_SMEM = PREP_WGT + PREP_WARPS * PREP_BUFS * PREP_ROW;
+
+// Packed f32 pairs on Blackwell's f32x2 pipe: each half rounded exactly like the scalar operation.
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<const unsigned long long*>(&a)), "l"(*reinterpret_cast<const unsigned long long*>(&b)));
+  return *reinterpret_cast<const float2*>(&d);
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<const unsigned long long*>(&a)), "l"(*reinterpret_cast<const unsigned long long*>(&b)),
+        "l"(*reinterpret_cast<const unsigned long long*>(&c)));
+  return *reinterpret_cast<const float2*>(&d);
+}
+__device__ __forceinline__ float2 unpack2(uint32_t w) { return make_float2(bf_lo(w), bf_hi(w)); }
+__device__ __forceinline__ uint32_t round2(float2 v) { return pack_bf16x2(v.x, v.y); }
+// max(|a|, |b|) of two bf16 values in one word, as f32 (exact: bf16 compares exactly)
+__device__ __forceinline__ float absmax_bf16x2(uint32_t w) {
+  return fmaxf(fabsf(bf_lo(w)), fabsf(bf_hi(w)));
+}
+__device__ __forceinline__ uint32_t absmax2_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a & 0x7fff7fffu), "r"(b & 0x7fff7fffu));
+  return d;
+}
+
+// A row's operands: the warp's shared-memory copy, or global memory when the row is not 16-byte
+// aligned for a bulk copy.
+struct SmemRow {
+  const u8* p;
+  __device__ __forceinline__ uint2 v2(int off) const { return *reinterpret_cast<const uint2*>(p + off); }
+  __device__ __forceinline__ uint32_t u32(int off) const { return *reinterpret_cast<const uint32_t*>(p + off); }
+};
+struct GlobalRow {
+  const u8* p;
+  __device__ __forceinline__ uint2 v2(int off) const { return ld_stream_v2(p + off); }
+  __device__ __forceinline__ uint32_t u32(int off) const { return ld_stream_u32(p + off); }
+};
 
 // One row of the latent-cache append (glm_glue.cu:196-287), run by ONE warp. Lane l holds exactly
 // the operands the reference's thread (w, l) holds for every warp w of its 256-thread block, so
 // the RMS sums are built in the reference's order (block_sum8); everything else is per element or
-// a max, which any order computes exactly.
-template <bool FP8>
-__device__ __forceinline__ void prep_row(const bf16* __restrict__ x, int lda, const bf16* __restrict__ g_q,
-                                         const bf16* __restrict__ g_kv, const bf16* __restrict__ rope,
-                                         const int* __restrict__ pos, const long long* __restrict__ slot,
-                                         u8* __restrict__ kv, u8* __restrict__ idx, const bf16* __restrict__ ik_w,
-                                         const bf16* __restrict__ ik_b, u8* __restrict__ qq, u8* __restrict__ qsf,
-                                         int sf_rows, int r, int l) {
-  const u8* row = reinterpret_cast<const u8*>(x + (size_t)r * lda);
-
-  // ---- the row's loads, all in flight at once
+// a max, which any order computes exactly. Weights come from shared memory as f32.
+template <bool FP8, class Row>
+__device__ __forceinline__ void prep_row(const Row& row, const float* __restrict__ wq, const float* __restrict__ wkv,
+                                         const float* __restrict__ wik, const float* __restrict__ wib,
+                                         const bf16* __restrict__ rope, int p, long long s, u8* __restrict__ kv,
+                                         u8* __restrict__ idx, u8* __restrict__ qq, u8* __restrict__ qsf, int sf_rows,
+                                         int r, int l) {
   uint2 qw[16];  // q_a columns kb * 128 + 4l .. + 3
 #pragma unroll
-  for (int kb = 0; kb < 16; ++kb) qw[kb] = ld_stream_v2(row + 2 * (kb * 128 + 4 * l));
+  for (int kb = 0; kb < 16; ++kb) qw[kb] = row.v2(2 * (kb * 128 + 4 * l));
   uint32_t kvw[8];  // kv_a columns 64w + 2l, + 1 (the reference's thread 32w + l)
 #pragma unroll
-  for (int w = 0; w < 8; ++w) kvw[w] = ld_stream_u32(row + 2 * (QL + 64 * w + 2 * l));
-  const uint32_t pew = ld_stream_u32(row + 2 * (QL + KVL + 2 * l));  // k_pe pair l
-  uint2 wkw = make_uint2(0u, 0u);
-  if (idx != nullptr) wkw = ld_stream_v2(row + 2 * (QL + KVL + 2 * HALF + 4 * l));  // wk columns 4l .. + 3
-  const long long s = slot[r];
+  for (int w = 0; w < 8; ++w) kvw[w] = row.u32(2 * (QL + 64 * w + 2 * l));
+  uint32_t csw = 0;  // rope[pos]: cs[2l], cs[2l + 1]
+  if (s >= 0) csw = __ldg(reinterpret_cast<const unsigned*>(rope + (size_t)p * 2 * HALF) + l);
 
-  // ---- RMS factors (glm_glue.cu:212-221): per-thread sequential partials, block_sum order
+  // ---- RMS factors (glm_glue.cu:212-221): per-thread sequential partials, block_sum order. Two
+  // virtual warps share an f32x2 accumulator; each half keeps its own sequence of FMAs.
   float part[8];
+  {
+    float2 acc[4];
 #pragma unroll
-  for (int w = 0; w < 8; ++w) {
-    const uint2 a = qw[2 * w], b = qw[2 * w + 1];
-    float ss = 0.f;
-    ss = __fmaf_rn(bf_lo(a.x), bf_lo(a.x), ss);
-    ss = __fmaf_rn(bf_hi(a.x), bf_hi(a.x), ss);
-    ss = __fmaf_rn(bf_lo(a.y), bf_lo(a.y), ss);
-    ss = __fmaf_rn(bf_hi(a.y), bf_hi(a.y), ss);
-    ss = __fmaf_rn(bf_lo(b.x), bf_lo(b.x), ss);
-    ss = __fmaf_rn(bf_hi(b.x), bf_hi(b.x), ss);
-    ss = __fmaf_rn(bf_lo(b.y), bf_lo(b.y), ss);
-    ss = __fmaf_rn(bf_hi(b.y), bf_hi(b.y), ss);
-    part[w] = ss;
+    for (int h = 0; h < 4; ++h) acc[h] = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const uint2 a = qw[4 * h + i], b = qw[4 * h + 2 + i];  // blocks 2(2h) + i and 2(2h + 1) + i
+        float2 v = make_float2(bf_lo(a.x), bf_lo(b.x));
+        acc[h] = fma2(v, v, acc[h]);
+        v = make_float2(bf_hi(a.x), bf_hi(b.x));
+        acc[h] = fma2(v, v, acc[h]);
+        v = make_float2(bf_lo(a.y), bf_lo(b.y));
+        acc[h] = fma2(v, v, acc[h]);
+        v = make_float2(bf_hi(a.y), bf_hi(b.y));
+        acc[h] = fma2(v, v, acc[h]);
+      }
+#pragma unroll
+    for (int h = 0; h < 4; ++h) part[2 * h] = acc[h].x, part[2 * h + 1] = acc[h].y;
   }
   const float rq = rsqrtf(block_sum8(part, l) / 2048.f + EPS);
 #pragma unroll
-  for (int w = 0; w < 8; ++w) {
-    const float a = bf_lo(kvw[w]), b = bf_hi(kvw[w]);
-    part[w] = __fmaf_rn(a, a, __fmul_rn(b, b));  // both squares exact: round(a^2 + b^2)
+  for (int h = 0; h < 4; ++h) {
+    const float2 a = make_float2(bf_lo(kvw[2 * h]), bf_lo(kvw[2 * h + 1]));
+    const float2 b = make_float2(bf_hi(kvw[2 * h]), bf_hi(kvw[2 * h + 1]));
+    const float2 t = fma2(a, a, mul2(b, b));  // both squares exact: round(a^2 + b^2)
+    part[2 * h] = t.x, part[2 * h + 1] = t.y;
   }
   const float rk = rsqrtf(block_sum8(part, l) / 512.f + EPS);
 
   // ---- q_c = bf16((q_a * rq) * g_q), e4m3 per 128 columns with UE8M0 scales (glm_glue.cu:222-230)
+  const float2 rq2 = make_float2(rq, rq);
   uint32_t yb[16][2];
   float am[16];
 #pragma unroll
   for (int kb = 0; kb < 16; ++kb) {
-    const uint2 g = __ldg(reinterpret_cast<const uint2*>(g_q + kb * 128 + 4 * l));
-    const uint2 q = qw[kb];
-    const float y0 = rnd(__fmul_rn(__fmul_rn(bf_lo(q.x), rq), bf_lo(g.x)));
-    const float y1 = rnd(__fmul_rn(__fmul_rn(bf_hi(q.x), rq), bf_hi(g.x)));
-    const float y2 = rnd(__fmul_rn(__fmul_rn(bf_lo(q.y), rq), bf_lo(g.y)));
-    const float y3 = rnd(__fmul_rn(__fmul_rn(bf_hi(q.y), rq), bf_hi(g.y)));
-    am[kb] = fmaxf(fmaxf(fabsf(y0), fabsf(y1)), fmaxf(fabsf(y2), fabsf(y3)));
-    yb[kb][0] = pack_bf16x2(y0, y1);  // exact: the values are bf16 already
-    yb[kb][1] = pack_bf16x2(y2, y3);
+    const float4 g = *reinterpret_cast<const float4*>(wq + kb * 128 + 4 * l);
+    yb[kb][0] = round2(mul2(mul2(unpack2(qw[kb].x), rq2), make_float2(g.x, g.y)));
+    yb[kb][1] = round2(mul2(mul2(unpack2(qw[kb].y), rq2), make_float2(g.z, g.w)));
+    const uint32_t m = absmax2_bf16x2(yb[kb][0], yb[kb][1]);
+    am[kb] = fmaxf(bf_lo(m), bf_hi(m));
   }
   unsigned e;
   const float inv = __frcp_rn(ue8m0(max16_scatter(am, l), 1e-10f, &e));  // lane l: block kb = l >> 1
@@ -141,9 +189,9 @@ __device__ __forceinline__ void prep_row(const bf16* __restrict__ x, int lda, co
 #pragma unroll
   for (int kb = 0; kb < 16; ++kb) {
     const float iv = __shfl_sync(FULL, inv, 2 * kb);
-    *reinterpret_cast<uint32_t*>(qrow + kb * 128 + 4 * l) =
-        fp8x4(__fmul_rn(bf_lo(yb[kb][0]), iv), __fmul_rn(bf_hi(yb[kb][0]), iv), __fmul_rn(bf_lo(yb[kb][1]), iv),
-              __fmul_rn(bf_hi(yb[kb][1]), iv));
+    const float2 iv2 = make_float2(iv, iv);
+    const float2 a = mul2(unpack2(yb[kb][0]), iv2), b = mul2(unpack2(yb[kb][1]), iv2);
+    *reinterpret_cast<uint32_t*>(qrow + kb * 128 + 4 * l) = fp8x4(a.x, a.y, b.x, b.y);
   }
   // DeepGEMM's packed scales: byte (kb & 3) of word (kb >> 2, r); lane q < 4 writes word q whole.
   unsigned word = 0;
@@ -153,21 +201,18 @@ __device__ __forceinline__ void prep_row(const bf16* __restrict__ x, int lda, co
 
   if (s < 0) return;  // no cache slot: nothing more to write (glm_glue.cu:231-232)
 
-  // ---- kv_norm = bf16((kv_a * rk) * g_kv) (glm_glue.cu:235)
-  const uint32_t csw = __ldg(reinterpret_cast<const unsigned*>(rope + (size_t)pos[r] * 2 * HALF) + l);
-  float k0[8], k1[8];
+  // ---- kv_norm = bf16((kv_a * rk) * g_kv) (glm_glue.cu:235), one bf16 pair a virtual thread
+  const float2 rk2 = make_float2(rk, rk);
+  uint32_t kn[8];
 #pragma unroll
-  for (int w = 0; w < 8; ++w) {
-    const uint32_t g = __ldg(reinterpret_cast<const unsigned*>(g_kv + 64 * w + 2 * l));
-    k0[w] = rnd(__fmul_rn(__fmul_rn(bf_lo(kvw[w]), rk), bf_lo(g)));
-    k1[w] = rnd(__fmul_rn(__fmul_rn(bf_hi(kvw[w]), rk), bf_hi(g)));
-  }
+  for (int w = 0; w < 8; ++w)
+    kn[w] = round2(mul2(mul2(unpack2(kvw[w]), rk2), *reinterpret_cast<const float2*>(wkv + 64 * w + 2 * l)));
   u8* dst = kv + s * (FP8 ? KV8 : KVB);
   if constexpr (FP8) {
     // tiles of 128 (two virtual warps), scale amax / 448, e4m3 satfinite (glm_glue.cu:238-247)
     float m8[8];
 #pragma unroll
-    for (int w = 0; w < 8; ++w) m8[w] = fmaxf(fabsf(k0[w]), fabsf(k1[w]));
+    for (int w = 0; w < 8; ++w) m8[w] = absmax_bf16x2(kn[w]);
     const float wm = max8_scatter(m8, l);                     // lane l: warp (l >> 2) & 7
     const float tm = fmaxf(wm, __shfl_xor_sync(FULL, wm, 4));  // lane l: tile (l >> 3) & 3
     const float sc = __fdiv_rn(tm, 448.f);
@@ -175,17 +220,19 @@ __device__ __forceinline__ void prep_row(const bf16* __restrict__ x, int lda, co
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
       const float iv = __shfl_sync(FULL, tinv, 8 * (w >> 1));
-      *reinterpret_cast<uint16_t*>(dst + 2 * (32 * w + l)) = fp8x2(__fmul_rn(k0[w], iv), __fmul_rn(k1[w], iv));
+      const float2 q = mul2(unpack2(kn[w]), make_float2(iv, iv));
+      *reinterpret_cast<uint16_t*>(dst + 2 * (32 * w + l)) = fp8x2(q.x, q.y);
     }
     const float sct = __shfl_sync(FULL, sc, 8 * (l & 3));
     if (l < 4) reinterpret_cast<float*>(dst + KVL)[l] = sct;
   } else {
 #pragma unroll
-    for (int w = 0; w < 8; ++w) *reinterpret_cast<uint32_t*>(dst + 4 * (32 * w + l)) = pack_bf16x2(k0[w], k1[w]);
+    for (int w = 0; w < 8; ++w) *reinterpret_cast<uint32_t*>(dst + 4 * (32 * w + l)) = kn[w];
   }
 
   // ---- k_pe rope, interleaved pairs (glm_glue.cu:252-257). The bf16 x bf16 products are exact in
   // f32, so this equals round(x1 c - x2 sn) however the reference contracted it.
+  const uint32_t pew = row.u32(2 * (QL + KVL + 2 * l));
   const uint32_t ca = __shfl_sync(FULL, csw, l >> 1), cb = __shfl_sync(FULL, csw, 16 + (l >> 1));
   {
     const float c = (l & 1) ? bf_hi(ca) : bf_lo(ca), sn = (l & 1) ? bf_hi(cb) : bf_lo(cb);
@@ -196,31 +243,30 @@ __device__ __forceinline__ void prep_row(const bf16* __restrict__ x, int lda, co
 
   // ---- indexer key (glm_glue.cu:258-286): LayerNorm (eps 1e-6), rope on dims 0..63, UE8M0 e4m3
   if (idx == nullptr) return;
-  const uint2 iw = __ldg(reinterpret_cast<const uint2*>(ik_w + 4 * l));
-  const uint2 ib = __ldg(reinterpret_cast<const uint2*>(ik_b + 4 * l));
+  const uint2 wkw = row.v2(2 * (QL + KVL + 2 * HALF + 4 * l));  // wk columns 4l .. + 3
+  const float4 kw = *reinterpret_cast<const float4*>(wik + 4 * l);
+  const float4 kbias = *reinterpret_cast<const float4*>(wib + 4 * l);
   const float k[4] = {bf_lo(wkw.x), bf_hi(wkw.x), bf_lo(wkw.y), bf_hi(wkw.y)};
-  const float kw[4] = {bf_lo(iw.x), bf_hi(iw.x), bf_lo(iw.y), bf_hi(iw.y)};
-  const float kbias[4] = {bf_lo(ib.x), bf_hi(ib.x), bf_lo(ib.y), bf_hi(ib.y)};
   const float mean = warp_sum(((k[0] + k[1]) + k[2]) + k[3]) / 128.f;
   float d[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) d[j] = __fsub_rn(k[j], mean);
-  // The f32 contractions of the reference's compiled code: d2 += d * d as one FMA a step,
-  // (d * rstd) * w + b with the last multiply fused, and the rope fusing each first product.
+  // The f32 contractions of the reference's compiled code (found by running it on 2^20 rows against
+  // every combination): d2 += d * d as one FMA a step; (d * rstd) * w + b with the last multiply
+  // fused; the rope as fma(e, c, -(o * sn)) and fma(e, sn, o * c).
   float d2 = 0.f;
 #pragma unroll
   for (int j = 0; j < 4; ++j) d2 = __fmaf_rn(d[j], d[j], d2);
   const float rstd = rsqrtf(warp_sum(d2) / 128.f + 1e-6f);
-  float n[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) n[j] = __fmaf_rn(__fmul_rn(d[j], rstd), kw[j], kbias[j]);
+  float n[4] = {__fmaf_rn(__fmul_rn(d[0], rstd), kw.x, kbias.x), __fmaf_rn(__fmul_rn(d[1], rstd), kw.y, kbias.y),
+                __fmaf_rn(__fmul_rn(d[2], rstd), kw.z, kbias.z), __fmaf_rn(__fmul_rn(d[3], rstd), kw.w, kbias.w)};
   const uint32_t csh = __shfl_sync(FULL, csw, (l + 16) & 31);  // cs[32 + 2l], cs[33 + 2l]
   if (l < 16) {
 #pragma unroll
     for (int j = 0; j < 4; j += 2) {
       const float c = j ? bf_hi(csw) : bf_lo(csw), sn = j ? bf_hi(csh) : bf_lo(csh), ev = n[j], od = n[j + 1];
       n[j] = __fmaf_rn(ev, c, -__fmul_rn(od, sn));
-      n[j + 1] = __fmaf_rn(od, c, __fmul_rn(ev, sn));
+      n[j + 1] = __fmaf_rn(ev, sn, __fmul_rn(od, c));
     }
   }
   const float amax = warp_max(fmaxf(fmaxf(fabsf(n[0]), fabsf(n[1])), fmaxf(fabsf(n[2]), fabsf(n[3]))));
@@ -233,6 +279,75 @@ __device__ __forceinline__ void prep_row(const bf16* __restrict__ x, int lda, co
   if (l == 0) reinterpret_cast<float*>(page + PAGE * ID)[i] = sc;
 }
 
+// The rows of a call, a warp at a time: warp g of the grid takes rows g, g + G, g + 2G, ... (G warps
+// in the grid). While it works on one row, the next one is already on its way: a 1-D bulk copy
+// (TMA) of the row's 5504 bytes (5248 on a shared layer, which has no wk) into the warp's other
+// shared-memory buffer, completing on that buffer's mbarrier. Rows that are not 16-byte aligned
+// (lda % 8 or x % 16) are read straight from global memory instead.
+template <bool FP8>
+__device__ __forceinline__ void prep_rows(const bf16* __restrict__ x, int lda, const bf16* __restrict__ g_q,
+                                          const bf16* __restrict__ g_kv, const bf16* __restrict__ rope,
+                                          const int* __restrict__ pos, const long long* __restrict__ slot,
+                                          u8* __restrict__ kv, u8* __restrict__ idx, const bf16* __restrict__ ik_w,
+                                          const bf16* __restrict__ ik_b, u8* __restrict__ qq, u8* __restrict__ qsf,
+                                          int sf_rows, int T) {
+  extern __shared__ __align__(128) u8 smem[];
+  __shared__ __align__(8) unsigned long long bar[PREP_WARPS][PREP_BUFS];
+  float* wq = reinterpret_cast<float*>(smem);
+  float* wkv = wq + QL;
+  float* wik = wkv + KVL;
+  float* wib = wik + ID;
+  const int tid = threadIdx.x, warp = tid >> 5, l = tid & 31;
+  for (int i = tid; i < QL; i += PREP_THREADS) wq[i] = __bfloat162float(g_q[i]);
+  for (int i = tid; i < KVL; i += PREP_THREADS) wkv[i] = __bfloat162float(g_kv[i]);
+  if (idx != nullptr)
+    for (int i = tid; i < ID; i += PREP_THREADS) wik[i] = __bfloat162float(ik_w[i]), wib[i] = __bfloat162float(ik_b[i]);
+  if (l == 0) {
+#pragma unroll
+    for (int b = 0; b < PREP_BUFS; ++b) mbar_init(smem_u32(&bar[warp][b]), 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
+
+  const int stride = gridDim.x * PREP_WARPS;
+  int r = blockIdx.x * PREP_WARPS + warp;
+  if (r >= T) return;
+  const bool bulk = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (lda & 7) == 0;
+  if (!bulk) {
+    for (; r < T; r += stride)
+      prep_row<FP8>(GlobalRow{reinterpret_cast<const u8*>(x + (size_t)r * lda)}, wq, wkv, wik, wib, rope, pos[r],
+                    slot[r], kv, idx, qq, qsf, sf_rows, r, l);
+    return;
+  }
+  const uint32_t bytes = idx != nullptr ? PREP_ROW : 2 * (QL + MLA);
+  u8* buf = smem + PREP_WGT + (size_t)warp * PREP_BUFS * PREP_ROW;
+  auto issue = [&](int b, int row) {
+    const uint32_t mb = smem_u32(&bar[warp][b]);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_arrive_expect_tx(mb, bytes);
+    tma_load_1d(smem_u32(buf + b * PREP_ROW), x + (size_t)row * lda, bytes, mb);
+  };
+  if (l == 0) issue(0, r);
+  for (int k = 0; r < T; ++k, r += stride) {
+    const int b = k & 1, rn = r + stride;
+    if (rn < T && l == 0) issue(b ^ 1, rn);  // that buffer's previous row is done (__syncwarp below)
+    const int p = pos[r];
+    const long long s = slot[r];
+    const bool ok = mbar_wait_bounded(smem_u32(&bar[warp][b]), (uint32_t)((k >> 1) & 1), WAIT_LIMIT_NS);
+    if (__any_sync(FULL, !ok)) {
+      // A copy never completed: flag it, wait (bounded) for the warp's copies in flight, and return.
+      if (l == 0) {
+        atomicOr(&g_fault, FAULT_WAIT_TIMEOUT);
+        if (rn < T)
+          mbar_wait_bounded(smem_u32(&bar[warp][b ^ 1]), (uint32_t)(((k + 1) >> 1) & 1), WAIT_LIMIT_NS);
+      }
+      return;
+    }
+    prep_row<FP8>(SmemRow{buf + b * PREP_ROW}, wq, wkv, wik, wib, rope, p, s, kv, idx, qq, qsf, sf_rows, r, l);
+    __syncwarp();
+  }
+}
+
 }  // namespace glmkv
 
 #define GLMKV_PREP_PARAMS                                                                                       \
@@ -241,26 +356,22 @@ __device__ __forceinline__ void prep_row(const bf16* __restrict__ x, int lda, co
       const long long *__restrict__ slot, glmkv::u8 *__restrict__ kv, glmkv::u8 *__restrict__ idx,             \
       const glmkv::bf16 *__restrict__ ik_w, const glmkv::bf16 *__restrict__ ik_b, glmkv::u8 *__restrict__ qq, \
       glmkv::u8 *__restrict__ qsf, int sf_rows, int T
-#define GLMKV_PREP_ARGS x, lda, g_q, g_kv, rope, pos, slot, kv, idx, ik_w, ik_b, qq, qsf, sf_rows
+#define GLMKV_PREP_ARGS x, lda, g_q, g_kv, rope, pos, slot, kv, idx, ik_w, ik_b, qq, qsf, sf_rows, T
 
 // `--kv bf16` append: row at kv + slot * 1152 (glm_glue.cu:294-296).
-//   grid ceil(T / 8), block 256: a warp a row
-extern "C" __global__ void __launch_bounds__(glmkv::PREP_THREADS) glm_mla_prep(GLMKV_PREP_PARAMS) {
-  const int r = blockIdx.x * (glmkv::PREP_THREADS / 32) + (threadIdx.x >> 5);
-  if (r < T) glmkv::prep_row<false>(GLMKV_PREP_ARGS, r, threadIdx.x & 31);
+//   persistent: grid = SMs x resident CTAs, block 256, dynamic smem PREP_SMEM (99,328 B)
+extern "C" __global__ void __launch_bounds__(glmkv::PREP_THREADS, 2) glm_mla_prep(GLMKV_PREP_PARAMS) {
+  glmkv::prep_rows<false>(GLMKV_PREP_ARGS);
 }
 // fp8_ds_mla append: row at kv + slot * 656 (glm_glue.cu:297-299).
-//   grid ceil(T / 8), block 256: a warp a row
-extern "C" __global__ void __launch_bounds__(glmkv::PREP_THREADS) glm_mla_prep_fp8(GLMKV_PREP_PARAMS) {
-  const int r = blockIdx.x * (glmkv::PREP_THREADS / 32) + (threadIdx.x >> 5);
-  if (r < T) glmkv::prep_row<true>(GLMKV_PREP_ARGS, r, threadIdx.x & 31);
+//   persistent: grid = SMs x resident CTAs, block 256, dynamic smem PREP_SMEM (99,328 B)
+extern "C" __global__ void __launch_bounds__(glmkv::PREP_THREADS, 2) glm_mla_prep_fp8(GLMKV_PREP_PARAMS) {
+  glmkv::prep_rows<true>(GLMKV_PREP_ARGS);
 }
 
 // ================================================================================================ page pipeline
 
 namespace glmkv {
-
-constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;  // a bounded wait gives up after one second
 
 struct StageMeta {
   unsigned long long row;  // first stream row of the page

@@ -238,3 +238,20 @@ def test_bad_page_is_skipped_and_flagged(cuda):
     assert torch.all(s[lo:hi] == 7.0)
     assert torch.equal(s[:lo].view(torch.int16), g[:lo].view(torch.int16))
     assert torch.equal(s[hi:c.ctx].view(torch.int16), g[hi:c.ctx].view(torch.int16))
+
+
+@needs_ref
+@pytest.mark.parametrize("lda", [2756, 2760])
+def test_append_rows_not_aligned_for_bulk_copy(cuda, lda):
+    """Rows whose start is not 16-byte aligned (lda % 8 != 0) take the direct-load path; lda 2760 the
+    bulk-copy one. Both bit-exact against the reference."""
+    from glmkv import workload as W
+
+    call = W.config("cfg0", seed=8)
+    case = LayerCase(call, "fp8", seed=8, zero_tiles=3, with_topk=False)
+    wide = np.zeros((case.T, lda), np.uint16)
+    wide[:, :case.x.shape[1]] = case.x
+    wide[:, case.x.shape[1]:] = 0x7FC0  # padding columns: NaN if anything read them
+    case.x, case.lda = wide, lda
+    got, ref = _run_both(case, cuda, full=True)
+    _assert_all_equal(got, ref, f"lda {lda}")
