@@ -308,24 +308,22 @@ def main():
     barrier()
     # per-kernel timing inside the timed region: one dequant launch a step (a different layer each
     # step), bracketed by two events on the launch stream
-    ev, step_no = [], [0]
+    ev, target = [], [None]
     layers = group.layers
 
     def hook(l, before):
-        if l != layers[step_no[0] % len(layers)]:
-            return
-        e = torch.cuda.Event(enable_timing=True)
-        e.record()
-        ev.append(e)
-        if not before:
-            step_no[0] += 1
+        if l == target[0]:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            ev.append(e)
 
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(ids, enabled=(rank == 0 and not a.no_clocks)) as clk:
         torch.cuda.synchronize()
         barrier()
         start.record()
-        for _ in range(a.steps):
+        for i in range(a.steps):
+            target[0] = layers[i % len(layers)]
             run(hook)
         end.record()
         torch.cuda.synchronize()

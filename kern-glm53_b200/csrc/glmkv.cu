@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -63,7 +64,35 @@ const DeviceInfo* device_info() {
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
-inline int launched() { return cudaGetLastError() == cudaSuccess ? GLMKV_OK : GLMKV_ERR_LAUNCH; }
+// Launches use programmatic stream serialization (PDL) unless GLMKV_PDL=0: every kernel waits in
+// pdl_wait() before its first global-memory access, so it may be scheduled while the previous kernel
+// on the stream drains, which hides the launch latency between the path's back-to-back kernels.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("GLMKV_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+int launch(void (*kernel)(KArgs...), int grid, int block, size_t smem, glmkv_stream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...) != cudaSuccess) {
+    cudaGetLastError();
+    return GLMKV_ERR_LAUNCH;
+  }
+  return GLMKV_OK;
+}
 
 template <bool FP8>
 int prep(const void* x, int lda, const void* g_q, const void* g_kv, const void* rope, const int32_t* pos,
@@ -80,11 +109,9 @@ int prep(const void* x, int lda, const void* g_q, const void* g_kv, const void* 
   const DeviceInfo* d = device_info();
   if (!d) return GLMKV_ERR_DEVICE;
   const int grid = std::min(d->sms * d->prep_ctas, (T + PREP_WARPS - 1) / PREP_WARPS);
-  auto k = FP8 ? glm_mla_prep_fp8 : glm_mla_prep;
-  k<<<grid, PREP_THREADS, PREP_SMEM, (cudaStream_t)stream>>>(
-      (const bf16*)x, lda, (const bf16*)g_q, (const bf16*)g_kv, (const bf16*)rope, pos, (const long long*)slot, (u8*)kv,
-      (u8*)idx, (const bf16*)ik_w, (const bf16*)ik_b, (u8*)qq, (u8*)qsf, sf_rows, T);
-  return launched();
+  return launch(FP8 ? glm_mla_prep_fp8 : glm_mla_prep, grid, PREP_THREADS, PREP_SMEM, stream, (const bf16*)x, lda,
+                (const bf16*)g_q, (const bf16*)g_kv, (const bf16*)rope, pos, (const long long*)slot, (u8*)kv, (u8*)idx,
+                (const bf16*)ik_w, (const bf16*)ik_b, (u8*)qq, (u8*)qsf, sf_rows, T);
 }
 
 }  // namespace
@@ -94,9 +121,8 @@ GLMKV_API int glmkv_plan(const int64_t* cu, const int32_t* seq_lens, int nseq, i
   if (T < 0 || nseq < 1) return GLMKV_ERR_ARG;
   if (T == 0) return GLMKV_OK;
   if (!cu || !seq_lens || !pos || !ks || !ke || !klen || !row_seq || !zero) return GLMKV_ERR_ARG;
-  glm_plan<<<(T + PLAN_THREADS - 1) / PLAN_THREADS, PLAN_THREADS, 0, (cudaStream_t)stream>>>(
-      (const long long*)cu, seq_lens, nseq, pos, ks, ke, klen, row_seq, zero, T);
-  return launched();
+  return launch(glm_plan, (T + PLAN_THREADS - 1) / PLAN_THREADS, PLAN_THREADS, 0, stream, (const long long*)cu, seq_lens,
+                nseq, pos, ks, ke, klen, row_seq, zero, T);
 }
 
 GLMKV_API int glmkv_mla_prep(const void* x, int lda, const void* g_q, const void* g_kv, const void* rope,
@@ -119,9 +145,8 @@ GLMKV_API int glmkv_idx_gather(const void* idx, const int32_t* block_table, int 
   if (!aligned(idx, 16) || !aligned(kg, 16) || !aligned(ksf, 4)) return GLMKV_ERR_ALIGN;
   const DeviceInfo* d = device_info();
   if (!d) return GLMKV_ERR_DEVICE;
-  glm_idx_gather<<<d->sms * d->ga_ctas, GA_THREADS, GA_SMEM, (cudaStream_t)stream>>>(
-      (const u8*)idx, block_table, max_pages, seq_lens, nseq, (u8*)kg, ksf);
-  return launched();
+  return launch(glm_idx_gather, d->sms * d->ga_ctas, GA_THREADS, GA_SMEM, stream, (const u8*)idx, block_table,
+                max_pages, seq_lens, nseq, (u8*)kg, ksf);
 }
 
 GLMKV_API int glmkv_kv_dequant(const void* kv, const int32_t* block_table, int max_pages, const int32_t* seq_lens,
@@ -132,9 +157,8 @@ GLMKV_API int glmkv_kv_dequant(const void* kv, const int32_t* block_table, int m
   if (!aligned(kv, 16) || !aligned(kvd, 16)) return GLMKV_ERR_ALIGN;
   const DeviceInfo* d = device_info();
   if (!d) return GLMKV_ERR_DEVICE;
-  glm_kv_dequant<<<d->sms * d->dq_ctas, DQ_THREADS, DQ_SMEM, (cudaStream_t)stream>>>(
-      (const u8*)kv, block_table, max_pages, seq_lens, nseq, (bf16*)kvd);
-  return launched();
+  return launch(glm_kv_dequant, d->sms * d->dq_ctas, DQ_THREADS, DQ_SMEM, stream, (const u8*)kv, block_table,
+                max_pages, seq_lens, nseq, (bf16*)kvd);
 }
 
 GLMKV_API int glmkv_topk_stream(int32_t* ind, const uint32_t* ks, const int32_t* klen, int32_t* tlen, int T,
@@ -143,8 +167,7 @@ GLMKV_API int glmkv_topk_stream(int32_t* ind, const uint32_t* ks, const int32_t*
   if (T == 0) return GLMKV_OK;
   if (!ind || !ks || !klen || !tlen) return GLMKV_ERR_ARG;
   if (!aligned(ind, 16)) return GLMKV_ERR_ALIGN;
-  glm_topk_stream<<<T, TK_THREADS, 0, (cudaStream_t)stream>>>(ind, ks, klen, tlen, T);
-  return launched();
+  return launch(glm_topk_stream, T, TK_THREADS, 0, stream, ind, ks, klen, tlen, T);
 }
 
 GLMKV_API int glmkv_topk_slots(int32_t* ind, const int32_t* block_table, int max_pages, const int32_t* row_seq,
@@ -153,8 +176,7 @@ GLMKV_API int glmkv_topk_slots(int32_t* ind, const int32_t* block_table, int max
   if (T == 0) return GLMKV_OK;
   if (!ind || !block_table || !row_seq || !klen || !tlen) return GLMKV_ERR_ARG;
   if (!aligned(ind, 16)) return GLMKV_ERR_ALIGN;
-  glm_topk_slots<<<T, TK_THREADS, 0, (cudaStream_t)stream>>>(ind, block_table, max_pages, row_seq, klen, tlen, T);
-  return launched();
+  return launch(glm_topk_slots, T, TK_THREADS, 0, stream, ind, block_table, max_pages, row_seq, klen, tlen, T);
 }
 
 GLMKV_API int glmkv_launch_shape(const char* entry, int T, int* grid, int* block, int* smem_bytes) {

@@ -38,17 +38,17 @@ enum : unsigned { FAULT_WAIT_TIMEOUT = 1u, FAULT_BAD_PAGE = 2u };
 
 __device__ __forceinline__ uint2 ld_stream_v2(const void* p) {
   uint2 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  asm("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
   return v;
 }
 __device__ __forceinline__ uint32_t ld_stream_u32(const void* p) {
   uint32_t v;
-  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
   return v;
 }
 __device__ __forceinline__ int4 ld_stream_v4(const void* p) {
   int4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0, %1, %2, %3}, [%4];"
+  asm("ld.global.nc.L1::no_allocate.v4.s32 {%0, %1, %2, %3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
   return v;
@@ -242,6 +242,15 @@ __device__ __forceinline__ void tma_load_1d(uint32_t dst, const void* src, uint3
                "l"(src), "r"(bytes), "r"(bar)
                : "memory");
 }
+
+// Programmatic dependent launch. A kernel launched with programmatic stream serialization may start
+// while the kernel before it on the stream is finishing; it must not touch global memory before
+// pdl_wait(), which returns once that kernel has completed and its writes are visible (at once when
+// the launch had no programmatic dependency). pdl_trigger() lets the next kernel start early; it is
+// issued only when every CTA of this grid is already resident, so early dependents never hold
+// resources that this grid's own CTAs still need.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // The pages of every sequence in order (kern-glm53 glm_glue.cu:360-371, 385-395): page j of
 // sequence s covers its rows [64 j, min(64 j + 64, len)) and lands at stream rows goff(s) + 64 j,
