@@ -123,25 +123,25 @@ struct GlobalRow {
 // One row of the latent-cache append (glm_glue.cu:196-287), run by ONE warp. Lane l holds exactly
 // the operands the reference's thread (w, l) holds for every warp w of its 256-thread block, so
 // the RMS sums are built in the reference's order (block_sum8); everything else is per element or
-// a max, which any order computes exactly. Weights come from shared memory as f32. The q, kv and
-// indexer-key chains are independent; they sit in one branch-free block (the indexer key is a
-// template choice, the cache writes are predicated on the slot) so their reductions overlap.
-template <bool FP8, bool IDX, class Row>
+// a max, which any order computes exactly. Weights come from shared memory as f32.
+template <bool FP8, class Row>
 __device__ __forceinline__ void prep_row(const Row& row, const float* __restrict__ wq, const float* __restrict__ wkv,
                                          const float* __restrict__ wik, const float* __restrict__ wib,
                                          const bf16* __restrict__ rope, int p, long long s, u8* __restrict__ kv,
                                          u8* __restrict__ idx, u8* __restrict__ qq, u8* __restrict__ qsf, int sf_rows,
                                          int r, int l) {
-  const bool cached = s >= 0;  // a row without a slot writes no cache (glm_glue.cu:231-232)
-  uint32_t kvw[8];             // kv_a columns 64w + 2l, + 1 (the reference's thread 32w + l)
+  uint2 qw[16];  // q_a columns kb * 128 + 4l .. + 3
+#pragma unroll
+  for (int kb = 0; kb < 16; ++kb) qw[kb] = row.v2(2 * (kb * 128 + 4 * l));
+  uint32_t kvw[8];  // kv_a columns 64w + 2l, + 1 (the reference's thread 32w + l)
 #pragma unroll
   for (int w = 0; w < 8; ++w) kvw[w] = row.u32(2 * (QL + 64 * w + 2 * l));
   uint32_t csw = 0;  // rope[pos]: cs[2l], cs[2l + 1]
-  if (cached) csw = __ldg(reinterpret_cast<const unsigned*>(rope + (size_t)p * 2 * HALF) + l);
+  if (s >= 0) csw = __ldg(reinterpret_cast<const unsigned*>(rope + (size_t)p * 2 * HALF) + l);
 
   // ---- RMS factors (glm_glue.cu:212-221): per-thread sequential partials, block_sum order. Two
   // virtual warps share an f32x2 accumulator; each half keeps its own sequence of FMAs.
-  float part[8], kpart[8];
+  float part[8];
   {
     float2 acc[4];
 #pragma unroll
@@ -150,8 +150,7 @@ __device__ __forceinline__ void prep_row(const Row& row, const float* __restrict
     for (int i = 0; i < 2; ++i)
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
-        // q_a blocks 2(2h) + i and 2(2h + 1) + i, columns 4l .. + 3
-        const uint2 a = row.v2(2 * ((4 * h + i) * 128 + 4 * l)), b = row.v2(2 * ((4 * h + 2 + i) * 128 + 4 * l));
+        const uint2 a = qw[4 * h + i], b = qw[4 * h + 2 + i];  // blocks 2(2h) + i and 2(2h + 1) + i
         float2 v = make_float2(bf_lo(a.x), bf_lo(b.x));
         acc[h] = fma2(v, v, acc[h]);
         v = make_float2(bf_hi(a.x), bf_hi(b.x));
@@ -164,22 +163,15 @@ __device__ __forceinline__ void prep_row(const Row& row, const float* __restrict
 #pragma unroll
     for (int h = 0; h < 4; ++h) part[2 * h] = acc[h].x, part[2 * h + 1] = acc[h].y;
   }
+  const float rq = rsqrtf(block_sum8(part, l) / 2048.f + EPS);
 #pragma unroll
   for (int h = 0; h < 4; ++h) {
     const float2 a = make_float2(bf_lo(kvw[2 * h]), bf_lo(kvw[2 * h + 1]));
     const float2 b = make_float2(bf_hi(kvw[2 * h]), bf_hi(kvw[2 * h + 1]));
     const float2 t = fma2(a, a, mul2(b, b));  // both squares exact: round(a^2 + b^2)
-    kpart[2 * h] = t.x, kpart[2 * h + 1] = t.y;
+    part[2 * h] = t.x, part[2 * h + 1] = t.y;
   }
-  // indexer key's LayerNorm mean (glm_glue.cu:259-263)
-  float k[4] = {0.f, 0.f, 0.f, 0.f}, mean = 0.f;
-  if constexpr (IDX) {
-    const uint2 wkw = row.v2(2 * (QL + KVL + 2 * HALF + 4 * l));  // wk columns 4l .. + 3
-    k[0] = bf_lo(wkw.x), k[1] = bf_hi(wkw.x), k[2] = bf_lo(wkw.y), k[3] = bf_hi(wkw.y);
-    mean = warp_sum(((k[0] + k[1]) + k[2]) + k[3]) / 128.f;
-  }
-  const float rq = rsqrtf(block_sum8(part, l) / 2048.f + EPS);
-  const float rk = rsqrtf(block_sum8(kpart, l) / 512.f + EPS);
+  const float rk = rsqrtf(block_sum8(part, l) / 512.f + EPS);
 
   // ---- q_c = bf16((q_a * rq) * g_q), e4m3 per 128 columns with UE8M0 scales (glm_glue.cu:222-230)
   const float2 rq2 = make_float2(rq, rq);
@@ -188,66 +180,13 @@ __device__ __forceinline__ void prep_row(const Row& row, const float* __restrict
 #pragma unroll
   for (int kb = 0; kb < 16; ++kb) {
     const float4 g = *reinterpret_cast<const float4*>(wq + kb * 128 + 4 * l);
-    const uint2 q = row.v2(2 * (kb * 128 + 4 * l));
-    yb[kb][0] = round2(mul2(mul2(unpack2(q.x), rq2), make_float2(g.x, g.y)));
-    yb[kb][1] = round2(mul2(mul2(unpack2(q.y), rq2), make_float2(g.z, g.w)));
+    yb[kb][0] = round2(mul2(mul2(unpack2(qw[kb].x), rq2), make_float2(g.x, g.y)));
+    yb[kb][1] = round2(mul2(mul2(unpack2(qw[kb].y), rq2), make_float2(g.z, g.w)));
     const uint32_t m = absmax2_bf16x2(yb[kb][0], yb[kb][1]);
     am[kb] = fmaxf(bf_lo(m), bf_hi(m));
   }
-  // ---- kv_norm = bf16((kv_a * rk) * g_kv) (glm_glue.cu:235), one bf16 pair a virtual thread
-  const float2 rk2 = make_float2(rk, rk);
-  uint32_t kn[8];
-#pragma unroll
-  for (int w = 0; w < 8; ++w)
-    kn[w] = round2(mul2(mul2(unpack2(kvw[w]), rk2), *reinterpret_cast<const float2*>(wkv + 64 * w + 2 * l)));
-  // ---- indexer key: the LayerNorm factor (glm_glue.cu:264-267). The f32 contractions are those of
-  // the reference's compiled code (found by running it on 2^20 rows against every combination):
-  // d2 += d * d as one FMA a step; (d * rstd) * w + b with the last multiply fused; the rope as
-  // fma(e, c, -(o * sn)) and fma(e, sn, o * c).
-  float d[4], rstd = 0.f;
-  if constexpr (IDX) {
-    float d2 = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) d[j] = __fsub_rn(k[j], mean), d2 = __fmaf_rn(d[j], d[j], d2);
-    rstd = rsqrtf(warp_sum(d2) / 128.f + 1e-6f);
-  }
-
   unsigned e;
   const float inv = __frcp_rn(ue8m0(max16_scatter(am, l), 1e-10f, &e));  // lane l: block kb = l >> 1
-  float sc = 0.f, tinv = 0.f;
-  if constexpr (FP8) {
-    // tiles of 128 (two virtual warps), scale amax / 448 (glm_glue.cu:238-244)
-    float m8[8];
-#pragma unroll
-    for (int w = 0; w < 8; ++w) m8[w] = absmax_bf16x2(kn[w]);
-    const float wm = max8_scatter(m8, l);                     // lane l: warp (l >> 2) & 7
-    const float tm = fmaxf(wm, __shfl_xor_sync(FULL, wm, 4));  // lane l: tile (l >> 3) & 3
-    sc = __fdiv_rn(tm, 448.f);
-    tinv = sc > 0.f ? __frcp_rn(sc) : 0.f;
-  }
-  float n[4];
-  float isc = 0.f;
-  if constexpr (IDX) {
-    const float4 kw = *reinterpret_cast<const float4*>(wik + 4 * l);
-    const float4 kbias = *reinterpret_cast<const float4*>(wib + 4 * l);
-    n[0] = __fmaf_rn(__fmul_rn(d[0], rstd), kw.x, kbias.x);
-    n[1] = __fmaf_rn(__fmul_rn(d[1], rstd), kw.y, kbias.y);
-    n[2] = __fmaf_rn(__fmul_rn(d[2], rstd), kw.z, kbias.z);
-    n[3] = __fmaf_rn(__fmul_rn(d[3], rstd), kw.w, kbias.w);
-    const uint32_t csh = __shfl_sync(FULL, csw, (l + 16) & 31);  // cs[32 + 2l], cs[33 + 2l]
-    if (l < 16) {
-#pragma unroll
-      for (int j = 0; j < 4; j += 2) {
-        const float c = j ? bf_hi(csw) : bf_lo(csw), sn = j ? bf_hi(csh) : bf_lo(csh), ev = n[j], od = n[j + 1];
-        n[j] = __fmaf_rn(ev, c, -__fmul_rn(od, sn));
-        n[j + 1] = __fmaf_rn(ev, sn, __fmul_rn(od, c));
-      }
-    }
-    unsigned ex;
-    isc = ue8m0(warp_max(fmaxf(fmaxf(fabsf(n[0]), fabsf(n[1])), fmaxf(fabsf(n[2]), fabsf(n[3])))), 1e-4f, &ex);
-  }
-
-  // ---- stores: q_c and its scales always; the cache row and indexer key when the row has a slot
   u8* qrow = qq + (size_t)r * QL;
 #pragma unroll
   for (int kb = 0; kb < 16; ++kb) {
@@ -262,42 +201,84 @@ __device__ __forceinline__ void prep_row(const Row& row, const float* __restrict
   for (int m = 0; m < 4; ++m) word |= __shfl_sync(FULL, e, 2 * (4 * (l & 3) + m)) << (8 * m);
   if (l < 4) *reinterpret_cast<unsigned*>(qsf + ((size_t)l * sf_rows + r) * 4) = word;
 
-  u8* dst = kv + (cached ? s : 0) * (FP8 ? KV8 : KVB);
+  if (s < 0) return;  // no cache slot: nothing more to write (glm_glue.cu:231-232)
+
+  // ---- kv_norm = bf16((kv_a * rk) * g_kv) (glm_glue.cu:235), one bf16 pair a virtual thread
+  const float2 rk2 = make_float2(rk, rk);
+  uint32_t kn[8];
+#pragma unroll
+  for (int w = 0; w < 8; ++w)
+    kn[w] = round2(mul2(mul2(unpack2(kvw[w]), rk2), *reinterpret_cast<const float2*>(wkv + 64 * w + 2 * l)));
+  u8* dst = kv + s * (FP8 ? KV8 : KVB);
   if constexpr (FP8) {
-    // e4m3 satfinite of kv_norm / its tile scale (glm_glue.cu:245-247)
+    // tiles of 128 (two virtual warps), scale amax / 448, e4m3 satfinite (glm_glue.cu:238-247)
+    float m8[8];
+#pragma unroll
+    for (int w = 0; w < 8; ++w) m8[w] = absmax_bf16x2(kn[w]);
+    const float wm = max8_scatter(m8, l);                     // lane l: warp (l >> 2) & 7
+    const float tm = fmaxf(wm, __shfl_xor_sync(FULL, wm, 4));  // lane l: tile (l >> 3) & 3
+    const float sc = __fdiv_rn(tm, 448.f);
+    const float tinv = sc > 0.f ? __frcp_rn(sc) : 0.f;
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
       const float iv = __shfl_sync(FULL, tinv, 8 * (w >> 1));
       const float2 q = mul2(unpack2(kn[w]), make_float2(iv, iv));
-      if (cached) *reinterpret_cast<uint16_t*>(dst + 2 * (32 * w + l)) = fp8x2(q.x, q.y);
+      *reinterpret_cast<uint16_t*>(dst + 2 * (32 * w + l)) = fp8x2(q.x, q.y);
     }
     const float sct = __shfl_sync(FULL, sc, 8 * (l & 3));
-    if (cached && l < 4) reinterpret_cast<float*>(dst + KVL)[l] = sct;
+    if (l < 4) reinterpret_cast<float*>(dst + KVL)[l] = sct;
   } else {
 #pragma unroll
-    for (int w = 0; w < 8; ++w)
-      if (cached) *reinterpret_cast<uint32_t*>(dst + 4 * (32 * w + l)) = kn[w];
+    for (int w = 0; w < 8; ++w) *reinterpret_cast<uint32_t*>(dst + 4 * (32 * w + l)) = kn[w];
   }
-  // k_pe rope, interleaved pairs (glm_glue.cu:252-257). The bf16 x bf16 products are exact in f32,
-  // so this equals round(x1 c - x2 sn) however the reference contracted it.
+
+  // ---- k_pe rope, interleaved pairs (glm_glue.cu:252-257). The bf16 x bf16 products are exact in
+  // f32, so this equals round(x1 c - x2 sn) however the reference contracted it.
   const uint32_t pew = row.u32(2 * (QL + KVL + 2 * l));
   const uint32_t ca = __shfl_sync(FULL, csw, l >> 1), cb = __shfl_sync(FULL, csw, 16 + (l >> 1));
   {
     const float c = (l & 1) ? bf_hi(ca) : bf_lo(ca), sn = (l & 1) ? bf_hi(cb) : bf_lo(cb);
     const float x1 = bf_lo(pew), x2 = bf_hi(pew);
-    const uint32_t pe = pack_bf16x2(__fmaf_rn(x1, c, -__fmul_rn(x2, sn)), __fmaf_rn(x2, c, __fmul_rn(x1, sn)));
-    if (cached) *reinterpret_cast<uint32_t*>(dst + (FP8 ? KVL + 16 : 2 * KVL) + 4 * l) = pe;
+    *reinterpret_cast<uint32_t*>(dst + (FP8 ? KVL + 16 : 2 * KVL) + 4 * l) =
+        pack_bf16x2(__fmaf_rn(x1, c, -__fmul_rn(x2, sn)), __fmaf_rn(x2, c, __fmul_rn(x1, sn)));
   }
-  if constexpr (IDX) {
-    // the key: e4m3 of n / its UE8M0 scale into the page-blocked indexer cache (glm_glue.cu:280-286)
-    if (cached) {
-      u8* page = idx + (size_t)(s / PAGE) * IDX_PAGE;
-      const int i = (int)(s % PAGE);
-      *reinterpret_cast<uint32_t*>(page + i * ID + 4 * l) =
-          fp8x4(__fdiv_rn(n[0], isc), __fdiv_rn(n[1], isc), __fdiv_rn(n[2], isc), __fdiv_rn(n[3], isc));
-      if (l == 0) reinterpret_cast<float*>(page + PAGE * ID)[i] = isc;
+
+  // ---- indexer key (glm_glue.cu:258-286): LayerNorm (eps 1e-6), rope on dims 0..63, UE8M0 e4m3
+  if (idx == nullptr) return;
+  const uint2 wkw = row.v2(2 * (QL + KVL + 2 * HALF + 4 * l));  // wk columns 4l .. + 3
+  const float4 kw = *reinterpret_cast<const float4*>(wik + 4 * l);
+  const float4 kbias = *reinterpret_cast<const float4*>(wib + 4 * l);
+  const float k[4] = {bf_lo(wkw.x), bf_hi(wkw.x), bf_lo(wkw.y), bf_hi(wkw.y)};
+  const float mean = warp_sum(((k[0] + k[1]) + k[2]) + k[3]) / 128.f;
+  float d[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) d[j] = __fsub_rn(k[j], mean);
+  // The f32 contractions of the reference's compiled code (found by running it on 2^20 rows against
+  // every combination): d2 += d * d as one FMA a step; (d * rstd) * w + b with the last multiply
+  // fused; the rope as fma(e, c, -(o * sn)) and fma(e, sn, o * c).
+  float d2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) d2 = __fmaf_rn(d[j], d[j], d2);
+  const float rstd = rsqrtf(warp_sum(d2) / 128.f + 1e-6f);
+  float n[4] = {__fmaf_rn(__fmul_rn(d[0], rstd), kw.x, kbias.x), __fmaf_rn(__fmul_rn(d[1], rstd), kw.y, kbias.y),
+                __fmaf_rn(__fmul_rn(d[2], rstd), kw.z, kbias.z), __fmaf_rn(__fmul_rn(d[3], rstd), kw.w, kbias.w)};
+  const uint32_t csh = __shfl_sync(FULL, csw, (l + 16) & 31);  // cs[32 + 2l], cs[33 + 2l]
+  if (l < 16) {
+#pragma unroll
+    for (int j = 0; j < 4; j += 2) {
+      const float c = j ? bf_hi(csw) : bf_lo(csw), sn = j ? bf_hi(csh) : bf_lo(csh), ev = n[j], od = n[j + 1];
+      n[j] = __fmaf_rn(ev, c, -__fmul_rn(od, sn));
+      n[j + 1] = __fmaf_rn(ev, sn, __fmul_rn(od, c));
     }
   }
+  const float amax = warp_max(fmaxf(fmaxf(fabsf(n[0]), fabsf(n[1])), fmaxf(fabsf(n[2]), fabsf(n[3]))));
+  unsigned ex;
+  const float sc = ue8m0(amax, 1e-4f, &ex);
+  u8* page = idx + (size_t)(s / PAGE) * IDX_PAGE;
+  const int i = (int)(s % PAGE);
+  *reinterpret_cast<uint32_t*>(page + i * ID + 4 * l) =
+      fp8x4(__fdiv_rn(n[0], sc), __fdiv_rn(n[1], sc), __fdiv_rn(n[2], sc), __fdiv_rn(n[3], sc));
+  if (l == 0) reinterpret_cast<float*>(page + PAGE * ID)[i] = sc;
 }
 
 // The rows of a call, a warp at a time: warp g of the grid takes rows g, g + G, g + 2G, ... (G warps
@@ -305,7 +286,7 @@ __device__ __forceinline__ void prep_row(const Row& row, const float* __restrict
 // (TMA) of the row's 5504 bytes (5248 on a shared layer, which has no wk) into the warp's other
 // shared-memory buffer, completing on that buffer's mbarrier. Rows that are not 16-byte aligned
 // (lda % 8 or x % 16) are read straight from global memory instead.
-template <bool FP8, bool IDX>
+template <bool FP8>
 __device__ __forceinline__ void prep_rows(const bf16* __restrict__ x, int lda, const bf16* __restrict__ g_q,
                                           const bf16* __restrict__ g_kv, const bf16* __restrict__ rope,
                                           const int* __restrict__ pos, const long long* __restrict__ slot,
@@ -328,7 +309,7 @@ __device__ __forceinline__ void prep_rows(const bf16* __restrict__ x, int lda, c
   pdl_wait();
   for (int i = tid; i < QL; i += PREP_THREADS) wq[i] = __bfloat162float(g_q[i]);
   for (int i = tid; i < KVL; i += PREP_THREADS) wkv[i] = __bfloat162float(g_kv[i]);
-  if constexpr (IDX)
+  if (idx != nullptr)
     for (int i = tid; i < ID; i += PREP_THREADS) wik[i] = __bfloat162float(ik_w[i]), wib[i] = __bfloat162float(ik_b[i]);
   __syncthreads();
 
@@ -338,11 +319,11 @@ __device__ __forceinline__ void prep_rows(const bf16* __restrict__ x, int lda, c
   const bool bulk = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (lda & 7) == 0;
   if (!bulk) {
     for (; r < T; r += stride)
-      prep_row<FP8, IDX>(GlobalRow{reinterpret_cast<const u8*>(x + (size_t)r * lda)}, wq, wkv, wik, wib, rope, pos[r],
-                         slot[r], kv, idx, qq, qsf, sf_rows, r, l);
+      prep_row<FP8>(GlobalRow{reinterpret_cast<const u8*>(x + (size_t)r * lda)}, wq, wkv, wik, wib, rope, pos[r],
+                    slot[r], kv, idx, qq, qsf, sf_rows, r, l);
     return;
   }
-  const uint32_t bytes = IDX ? PREP_ROW : 2 * (QL + MLA);
+  const uint32_t bytes = idx != nullptr ? PREP_ROW : 2 * (QL + MLA);
   u8* buf = smem + PREP_WGT + (size_t)warp * PREP_BUFS * PREP_ROW;
   auto issue = [&](int b, int row) {
     const uint32_t mb = smem_u32(&bar[warp][b]);
@@ -369,7 +350,7 @@ __device__ __forceinline__ void prep_rows(const bf16* __restrict__ x, int lda, c
       }
       return;
     }
-    prep_row<FP8, IDX>(SmemRow{buf + b * PREP_ROW}, wq, wkv, wik, wib, rope, p, s, kv, idx, qq, qsf, sf_rows, r, l);
+    prep_row<FP8>(SmemRow{buf + b * PREP_ROW}, wq, wkv, wik, wib, rope, p, s, kv, idx, qq, qsf, sf_rows, r, l);
     __syncwarp();
     p = pn, s = sn;
   }
@@ -388,18 +369,12 @@ __device__ __forceinline__ void prep_rows(const bf16* __restrict__ x, int lda, c
 // `--kv bf16` append: row at kv + slot * 1152 (glm_glue.cu:294-296).
 //   persistent: grid = SMs x resident CTAs, block 256, dynamic smem PREP_SMEM (99,328 B)
 extern "C" __global__ void __launch_bounds__(glmkv::PREP_THREADS, 2) glm_mla_prep(GLMKV_PREP_PARAMS) {
-  if (idx != nullptr)
-    glmkv::prep_rows<false, true>(GLMKV_PREP_ARGS);
-  else
-    glmkv::prep_rows<false, false>(GLMKV_PREP_ARGS);
+  glmkv::prep_rows<false>(GLMKV_PREP_ARGS);
 }
 // fp8_ds_mla append: row at kv + slot * 656 (glm_glue.cu:297-299).
 //   persistent: grid = SMs x resident CTAs, block 256, dynamic smem PREP_SMEM (99,328 B)
 extern "C" __global__ void __launch_bounds__(glmkv::PREP_THREADS, 2) glm_mla_prep_fp8(GLMKV_PREP_PARAMS) {
-  if (idx != nullptr)
-    glmkv::prep_rows<true, true>(GLMKV_PREP_ARGS);
-  else
-    glmkv::prep_rows<true, false>(GLMKV_PREP_ARGS);
+  glmkv::prep_rows<true>(GLMKV_PREP_ARGS);
 }
 
 // ================================================================================================ page pipeline
