@@ -97,6 +97,12 @@ int glmkv_topk_slots(int32_t* ind, const int32_t* block_table, int max_pages, co
  * generator (kern-glm53 scripts/gen.py:95-135, 172-177). */
 int glmkv_launch_shape(const char* entry, int T, int* grid, int* block, int* smem_bytes);
 
+/* Self-test of the bounded wait the page pipelines use: a kernel waits on a barrier that nothing
+ * completes, gives up after `limit_ns` (at most one second), sets fault bit 1 and writes the time it
+ * waited to the device word `waited_ns`. Lets a test check the timeout path without a fault. No
+ * counterpart in the reference. */
+int glmkv_selftest_wait(uint64_t limit_ns, uint32_t* waited_ns, glmkv_stream_t stream);
+
 /* Device-side fault bits of the current device's module (1: a bounded wait gave up; 2: a block
  * table named a negative page, which was skipped). Synchronises the device; clears the word when
  * `clear` is non-zero. No counterpart in the reference, whose kernels report nothing. */

@@ -203,6 +203,12 @@ GLMKV_API int glmkv_launch_shape(const char* entry, int T, int* grid, int* block
   return GLMKV_OK;
 }
 
+GLMKV_API int glmkv_selftest_wait(uint64_t limit_ns, uint32_t* waited_ns, glmkv_stream_t stream) {
+  if (!waited_ns || limit_ns == 0 || limit_ns > 1000000000ull) return GLMKV_ERR_ARG;
+  glmkv_wait_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>((unsigned long long)limit_ns, waited_ns);
+  return cudaGetLastError() == cudaSuccess ? GLMKV_OK : GLMKV_ERR_LAUNCH;
+}
+
 GLMKV_API int glmkv_fault_flags(uint32_t* flags, int clear) {
   if (!flags) return GLMKV_ERR_ARG;
   if (cudaDeviceSynchronize() != cudaSuccess ||

@@ -602,3 +602,19 @@ extern "C" __global__ void __launch_bounds__(glmkv::TK_THREADS)
   }
   if (threadIdx.x == 0) tlen[r] = min(klen[r], TOPK);
 }
+
+// Self-test of the bounded wait every pipeline uses: one thread waits on an mbarrier that nothing
+// ever arrives on, gives up after `limit_ns`, sets FAULT_WAIT_TIMEOUT and returns. No counterpart
+// in the reference.
+//   grid 1, block 32
+extern "C" __global__ void glmkv_wait_selftest_kernel(unsigned long long limit_ns, unsigned* __restrict__ waited_ns) {
+  using namespace glmkv;
+  __shared__ __align__(8) unsigned long long bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(smem_u32(&bar), 1);
+  mbar_init_fence();
+  const uint64_t t0 = global_ns();
+  if (!mbar_wait_bounded(smem_u32(&bar), 0u, limit_ns)) atomicOr(&g_fault, FAULT_WAIT_TIMEOUT);
+  const uint64_t dt = global_ns() - t0;
+  *waited_ns = dt > 0xffffffffull ? 0xffffffffu : (unsigned)dt;
+}

@@ -68,3 +68,13 @@ def test_host_side_argument_checks(built_lib):
     with pytest.raises(glmkv.GlmKvError):
         _lib.call("glmkv_topk_stream", A + 4, A, A, A, 8, None)
     assert "misaligned" in glmkv.strerror(_lib.ERR_ALIGN)
+
+
+def test_selftest_wait_rejects_bad_limits_on_the_host(built_lib):
+    import glmkv
+    from glmkv import _lib
+
+    L = glmkv.lib()
+    assert L.glmkv_selftest_wait(0, 0x10000, None) == _lib.ERR_ARG
+    assert L.glmkv_selftest_wait(2_000_000_000, 0x10000, None) == _lib.ERR_ARG
+    assert L.glmkv_selftest_wait(1000, None, None) == _lib.ERR_ARG
