@@ -54,6 +54,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--no-next-rows", action="store_true", help="skip timing the rows beside the path (glm_q_post)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     return ap.parse_args()
 
@@ -216,6 +217,52 @@ def run_call_reference(group, meta, inputs, ind, ctx, on_dequant=None):
         ref.kv_dequant(p(group.kv[l]), p(meta.block_table), mp, p(meta.seq_lens), nseq, p(group.kvd), ctx)
         if on_dequant:
             on_dequant(l, False)
+
+
+# ------------------------------------------------------------------------------------------ next rows
+
+def next_rows(torch, impl, T, dev, reps=10):
+    """The rows beside the path (glm_q_post on an indexer and a shared layer of the same call),
+    timed with CUDA events: the mean of `reps` launches after two warm-up launches."""
+    from glmkv import traffic
+    from glmkv import workload as W
+
+    import glmkv
+    g = torch.Generator(device=dev).manual_seed(5)
+    ldb = 64 * 256 + 32 * 128
+    qb = torch.randn(T, ldb, device=dev, generator=g).to(torch.bfloat16)
+    rope = torch.from_numpy(W.rope_table(1 << 16).view(np.int16)).to(dev).view(torch.bfloat16)
+    pos = torch.randint(0, 1 << 16, (T,), device=dev, generator=g, dtype=torch.int32)
+    qmla = torch.empty(T * 64 * 576, dtype=torch.bfloat16, device=dev)
+    iq = torch.empty(T * 32 * 128, dtype=torch.uint8, device=dev)
+    iw = torch.randn(T * 32, device=dev, generator=g).to(torch.bfloat16)
+    wout = torch.empty(T * 32, dtype=torch.float32, device=dev)
+    out = {}
+    for full in (True, False):
+        if impl == "glmkv":
+            if full:
+                fn = lambda: glmkv.q_post_full(qb, ldb, rope, pos, qmla, iq, iw, wout, 1, T)
+            else:
+                fn = lambda: glmkv.q_post_shared(qb, ldb, rope, pos, qmla, 0, T)
+        else:
+            from oracle import ref
+            p = lambda t: t.data_ptr()
+            fn = lambda: ref.q_post(p(qb), ldb, p(rope), p(pos), p(qmla), p(iq) if full else None,
+                                    p(iw) if full else None, p(wout) if full else None, int(full), T)
+        for _ in range(2):
+            fn()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(reps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        us = s.elapsed_time(e) / reps * 1e3
+        nbytes = traffic.q_post(T, full)
+        out["indexer_layer" if full else "shared_layer"] = {"us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1),
+                                                            "algorithmic_bytes": nbytes}
+    return {"glm_q_post": {"rows": T, **out}}
 
 
 # ------------------------------------------------------------------------------------------ CPU baseline
@@ -440,6 +487,8 @@ def main():
                                "seq_lens, block_table, slot_mapping copied from pinned host memory each step and "
                                "tlen read back" if a.impl == "glmkv" else
                                "reference kernels (oracle/_ref) with the same host copies"}
+    if not a.no_next_rows:
+        line["next_rows"] = next_rows(torch, a.impl, call.T, dev)
     if a.impl == "reference":
         line["cpu_baseline"] = {"value": line["value"], "unit": "GB/s", "cores": 1, "kind": "reference",
                                 "sample": "the whole workload: the reference's glue kernels (kern-glm53 "

@@ -89,9 +89,20 @@ int glmkv_topk_stream(int32_t* ind, const uint32_t* ks, const int32_t* klen, int
 int glmkv_topk_slots(int32_t* ind, const int32_t* block_table, int max_pages, const int32_t* row_seq,
                      const int32_t* klen, int32_t* tlen, int T, glmkv_stream_t stream);
 
+/* After the q_b GEMM: the rope of each head's q_pe into the tail of the absorbed query qmla
+ * [T, 64, 576] bf16 and, when `full`, the indexer query: rope on its first 64 dims, e4m3 per
+ * (row, head) into iq [T, 32, 128] with a UE8M0 scale, and the head weight
+ * wout [T, 32] f32 = ((iw * scale) * 128^-0.5) * 32^-0.5.
+ * Replaces ops `q_post_full` / `q_post_shared` -> glm_q_post (kern-glm53 scripts/gen.py:117-123;
+ * source/glm_glue.cu:306-351). qb [T, ldb] bf16: 64 heads of nope 192 | pe 64, then 32 indexer heads
+ * of 128. iq, iw, wout may be NULL when full == 0. Needs qb and qmla 16-byte aligned, ldb % 8 == 0,
+ * rope 8-byte aligned. */
+int glmkv_q_post(const void* qb, int ldb, const void* rope, const int32_t* pos, void* qmla, void* iq, const void* iw,
+                 float* wout, int full, int T, glmkv_stream_t stream);
+
 /* The launch shape (grid x, block x, dynamic shared memory bytes) libglmkv uses for the kernel
  * `entry` ("glm_plan", "glm_mla_prep", "glm_mla_prep_fp8", "glm_idx_gather", "glm_kv_dequant",
- * "glm_topk_stream", "glm_topk_slots") on the current device for a call of T fresh rows: what a kern
+ * "glm_topk_stream", "glm_topk_slots", "glm_q_post") on the current device for a call of T fresh rows: what a kern
  * manifest's `impl.launches` entry for the cubin must use. The persistent page kernels depend on the
  * device's SM count only. No counterpart in the reference, whose shapes are fixed in its manifest
  * generator (kern-glm53 scripts/gen.py:95-135, 172-177). */

@@ -179,11 +179,26 @@ GLMKV_API int glmkv_topk_slots(int32_t* ind, const int32_t* block_table, int max
   return launch(glm_topk_slots, T, TK_THREADS, 0, stream, ind, block_table, max_pages, row_seq, klen, tlen, T);
 }
 
+GLMKV_API int glmkv_q_post(const void* qb, int ldb, const void* rope, const int32_t* pos, void* qmla, void* iq,
+                           const void* iw, float* wout, int full, int T, glmkv_stream_t stream) {
+  if (T < 0) return GLMKV_ERR_ARG;
+  if (T == 0) return GLMKV_OK;
+  if (!qb || !rope || !pos || !qmla || (full && (!iq || !iw || !wout))) return GLMKV_ERR_ARG;
+  if (ldb < HEADS * QHD + (full ? IH * ID : 0)) return GLMKV_ERR_ARG;
+  if (ldb % 8 || !aligned(qb, 16) || !aligned(qmla, 16) || !aligned(rope, 8) ||
+      (full && (!aligned(iq, 4) || !aligned(wout, 4) || !aligned(iw, 2))))
+    return GLMKV_ERR_ALIGN;
+  return launch(glm_q_post, (T + QP_WARPS - 1) / QP_WARPS, QP_THREADS, 0, stream, (const bf16*)qb, ldb,
+                (const bf16*)rope, pos, (bf16*)qmla, (u8*)iq, (const bf16*)iw, wout, full, T);
+}
+
 GLMKV_API int glmkv_launch_shape(const char* entry, int T, int* grid, int* block, int* smem_bytes) {
   if (!entry || !grid || !block || !smem_bytes || T < 0) return GLMKV_ERR_ARG;
   const auto is = [entry](const char* s) { return strcmp(entry, s) == 0; };
   if (is("glm_plan")) {
     *grid = (T + PLAN_THREADS - 1) / PLAN_THREADS, *block = PLAN_THREADS, *smem_bytes = 0;
+  } else if (is("glm_q_post")) {
+    *grid = (T + QP_WARPS - 1) / QP_WARPS, *block = QP_THREADS, *smem_bytes = 0;
   } else if (is("glm_topk_stream") || is("glm_topk_slots")) {
     *grid = T, *block = TK_THREADS, *smem_bytes = 0;
   } else if (is("glm_kv_dequant") || is("glm_idx_gather") || is("glm_mla_prep") || is("glm_mla_prep_fp8")) {

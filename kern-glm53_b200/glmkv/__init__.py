@@ -6,7 +6,8 @@ dequant, the top-k row plans). The kernels are CUDA in ``libglmkv.so`` (C ABI: `
 this package binds them with ctypes and uses PyTorch only to own device memory.
 """
 from ._lib import CUBIN_PATH, LIB_PATH, GlmKvError, fault_flags, launch_shape, lib, strerror
-from .ops import (idx_gather, kv_dequant, mla_prep_full, mla_prep_shared, plan, topk_slots, topk_stream)
+from .ops import (idx_gather, kv_dequant, mla_prep_full, mla_prep_shared, plan, q_post_full, q_post_shared, topk_slots,
+                  topk_stream)
 
 __all__ = ["CUBIN_PATH", "LIB_PATH", "GlmKvError", "fault_flags", "launch_shape", "lib", "strerror", "plan", "mla_prep_full",
-           "mla_prep_shared", "idx_gather", "kv_dequant", "topk_stream", "topk_slots"]
+           "mla_prep_shared", "idx_gather", "kv_dequant", "topk_stream", "topk_slots", "q_post_full", "q_post_shared"]

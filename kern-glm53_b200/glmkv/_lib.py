@@ -19,6 +19,7 @@ SIGNATURES = {
     "glmkv_kv_dequant": [P, P, I, P, I, P, P],
     "glmkv_topk_stream": [P, P, P, P, I, P],
     "glmkv_topk_slots": [P, P, I, P, P, P, I, P],
+    "glmkv_q_post": [P, I, P, P, P, P, P, P, I, I, P],
     "glmkv_launch_shape": [ctypes.c_char_p, I, P, P, P],
     "glmkv_selftest_wait": [ctypes.c_uint64, P, P],
     "glmkv_fault_flags": [P, I],

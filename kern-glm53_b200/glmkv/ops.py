@@ -17,6 +17,9 @@ by the op's scalars, exactly in the manifest's parameter order, and enqueues one
     topk_stream      ind, ks, klen, tlen, T                 (130-132)     glm_topk_stream
     topk_slots       ind, block_table, max_pages, row_seq, klen, tlen, T  glm_topk_slots
                                                             (127-129)
+    q_post_full      qb, ldb, rope, pos, qmla, iq, iw, wout, full, T       glm_q_post
+                                                            (117-119)
+    q_post_shared    the same without iq, iw, wout (nulled, 120-123)       glm_q_post
 
 Errors (null or misaligned buffers, sizes out of range, a failed launch) raise ``GlmKvError``.
 """
@@ -104,3 +107,16 @@ def topk_slots(ind, block_table, max_pages, row_seq, klen, tlen, T, stream=None)
     _lib.call("glmkv_topk_slots", _ptr(ind, "i32", "ind"), _ptr(block_table, "i32", "block_table"), int(max_pages),
               _ptr(row_seq, "i32", "row_seq"), _ptr(klen, "i32", "klen"), _ptr(tlen, "i32", "tlen"), int(T),
               _stream(stream))
+
+
+def q_post_full(qb, ldb, rope, pos, qmla, iq, iw, wout, full, T, stream=None):
+    """The q_pe rope and, when `full`, the indexer query and head weights (op `q_post_full`)."""
+    _lib.call("glmkv_q_post", _ptr(qb, "bf16", "qb"), int(ldb), _ptr(rope, "bf16", "rope"), _ptr(pos, "i32", "pos"),
+              _ptr(qmla, "bf16", "qmla"), _ptr(iq, "u8", "iq"), _ptr(iw, "bf16", "iw"), _ptr(wout, "f32", "wout"),
+              int(full), int(T), _stream(stream))
+
+
+def q_post_shared(qb, ldb, rope, pos, qmla, full, T, stream=None):
+    """The q_pe rope of a shared layer (op `q_post_shared`, iq / iw / wout null)."""
+    _lib.call("glmkv_q_post", _ptr(qb, "bf16", "qb"), int(ldb), _ptr(rope, "bf16", "rope"), _ptr(pos, "i32", "pos"),
+              _ptr(qmla, "bf16", "qmla"), None, None, None, int(full), int(T), _stream(stream))

@@ -13,6 +13,12 @@ tokens (prefix + fresh) of the call's sequences.
     mla_prep (bf16 row)     fresh row      as above                      kv 1152 instead of 656    +496
     topk_stream/topk_slots  fresh row      8192 ind + 8 (ks/row, klen)   8192 ind + 4 tlen         16396
     plan                    fresh row      (cu, seq_lens: per call)      24 (six i32 / u32)        24
+
+The next rows, around the path:
+
+    q_post, indexer layer   fresh row      8192 q_pe + 8192 index query  8192 qmla tails + 4096    28996
+                                           + 128 rope + 4 + 64 iw        iq + 128 wout
+    q_post, shared layer    fresh row      8192 + 128 + 4                8192                      16516
 """
 QL, KVL, ROPE, ID, TOPK = 2048, 512, 64, 128, 2048
 
@@ -48,3 +54,7 @@ def layer(T, ctx, full, kv_dtype="fp8"):
     if kv_dtype == "fp8":
         b += kv_dequant(ctx)
     return b
+
+
+def q_post(T, full=True):
+    return (28996 if full else 16516) * T

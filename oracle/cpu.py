@@ -24,6 +24,7 @@ def lib():
         _lib.orc_kv_dequant.argtypes = [P, P, I, P, I, P]
         _lib.orc_topk_stream.argtypes = [P, P, P, P, I]
         _lib.orc_topk_slots.argtypes = [P, P, I, P, P, P, I]
+        _lib.orc_q_post.argtypes = [P, I, P, P, P, P, P, P, I, I]
         _lib.orc_bf16_from_f32.argtypes = [P, P, ctypes.c_long]
         _lib.orc_e4m3_from_f32.argtypes = [P, P, ctypes.c_long]
         _lib.orc_f32_from_e4m3.argtypes = [P, P, ctypes.c_long]
@@ -105,3 +106,8 @@ def f32_from_e4m3(x):
     y = np.empty(x.shape, np.float32)
     lib().orc_f32_from_e4m3(_p(x), _p(y), x.size)
     return y
+
+
+def q_post(qb, ldb, rope, pos, qmla, iq, iw, wout, full, T):
+    lib().orc_q_post(_p(qb, np.uint16), ldb, _p(rope, np.uint16), _p(pos, np.int32), _p(qmla, np.uint16),
+                     _p(iq, np.uint8), _p(iw, np.uint16), _p(wout, np.float32), int(bool(full)), T)

@@ -380,6 +380,53 @@ void orc_topk_slots(int32_t* ind, const int32_t* block_table, int max_pages, con
   }
 }
 
+/* ---------------------------------------------------------------- glm_q_post */
+
+#define HEADS 64
+#define QHD 256
+#define NOPE 192
+#define IH 32
+
+/* glm_glue.cu:301-351: the q_pe rope into the tail of each head of qmla [T, 64, 576], and on full
+ * layers the indexer query: rope on its first 64 dims, e4m3 per (row, head) with a UE8M0 scale
+ * (eps 1e-4), and the head weight w = ((f32(iw) * sc) * 128^-0.5) * 32^-0.5. Every rope product is
+ * bf16 x bf16, exact in f32, so no contraction can change a bit. */
+void orc_q_post(const uint16_t* qb, int ldb, const uint16_t* rope, const int32_t* pos, uint16_t* qmla, uint8_t* iq,
+                const uint16_t* iw, float* wout, int full, int T) {
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < T; ++r) {
+    const uint16_t* row = qb + (size_t)r * ldb;
+    const uint16_t* cs = rope + (size_t)pos[r] * 2 * HALF;
+    for (int h = 0; h < HEADS; ++h)
+      for (int pr = 0; pr < HALF; ++pr) {
+        const float x1 = bf16_f(row[h * QHD + NOPE + 2 * pr]), x2 = bf16_f(row[h * QHD + NOPE + 2 * pr + 1]);
+        const float c = bf16_f(cs[pr]), sn = bf16_f(cs[HALF + pr]);
+        uint16_t* d = qmla + ((size_t)r * HEADS + h) * MLA + KVL + 2 * pr;
+        d[0] = f_bf16(x1 * c - x2 * sn);
+        d[1] = f_bf16(x2 * c + x1 * sn);
+      }
+    if (!full) continue;
+    for (int ih = 0; ih < IH; ++ih) {
+      float v[ID], amax = 0.f;
+      for (int j = 0; j < ID; ++j) v[j] = bf16_f(row[HEADS * QHD + ih * ID + j]);
+      for (int pr = 0; pr < HALF; ++pr) {
+        const float c = bf16_f(cs[pr]), sn = bf16_f(cs[HALF + pr]), e = v[2 * pr], o = v[2 * pr + 1];
+        v[2 * pr] = e * c - o * sn;
+        v[2 * pr + 1] = o * c + e * sn;
+      }
+      for (int j = 0; j < ID; ++j) amax = fmaxf(amax, fabsf(v[j]));
+      uint8_t e;
+      const float sc = ue8m0(amax, 1e-4f, &e);
+      for (int j = 0; j < ID; ++j) iq[((size_t)r * IH + ih) * ID + j] = f_e4m3(v[j] / sc);
+      float x = bf16_f(iw[(size_t)r * IH + ih]);
+      x *= sc;
+      x *= 0.08838834764831845f;
+      x *= 0.17677669529663687f;
+      wout[(size_t)r * IH + ih] = x;
+    }
+  }
+}
+
 /* ---------------------------------------------------------------- helpers exported for tests */
 
 void orc_bf16_from_f32(const float* x, uint16_t* y, long n) {

@@ -33,6 +33,7 @@ def lib():
         _lib.ref_glm_kv_dequant.argtypes = [P, P, I, P, I, P, I, P]
         _lib.ref_glm_topk_stream.argtypes = [P, P, P, P, I, P]
         _lib.ref_glm_topk_slots.argtypes = [P, P, I, P, P, P, I, P]
+        _lib.ref_glm_q_post.argtypes = [P, I, P, P, P, P, P, P, I, I, P]
     return _lib
 
 
@@ -65,3 +66,7 @@ def topk_stream(ind, ks, klen, tlen, T, stream=0):
 
 def topk_slots(ind, block_table, max_pages, row_seq, klen, tlen, T, stream=0):
     _check(lib().ref_glm_topk_slots(ind, block_table, max_pages, row_seq, klen, tlen, T, stream), "glm_topk_slots")
+
+
+def q_post(qb, ldb, rope, pos, qmla, iq, iw, wout, full, T, stream=0):
+    _check(lib().ref_glm_q_post(qb, ldb, rope, pos, qmla, iq, iw, wout, int(bool(full)), T, stream), "glm_q_post")

@@ -12,6 +12,7 @@
 //   glm_kv_dequant     grid ceil(ctx / 64) + seqs, block 256
 //   glm_topk_stream    grid T,             block 256
 //   glm_topk_slots     grid T,             block 256
+//   glm_q_post         grid T,             block 256 (gen.py:117-123)
 // `ctx` is the manifest's launch variable (the sum of seq_lens); the caller passes it.
 #include <cuda_runtime.h>
 
@@ -70,5 +71,12 @@ REF_API int ref_glm_topk_slots(int* ind, const int* block_table, int max_pages, 
                                int* tlen, int T, void* stream) {
   if (T <= 0) return 0;
   glm_topk_slots<<<T, 256, 0, (cudaStream_t)stream>>>(ind, block_table, max_pages, row_seq, klen, tlen, T);
+  return ref_status();
+}
+
+REF_API int ref_glm_q_post(const bf16* qb, int ldb, const bf16* rope, const int* pos, bf16* qmla, u8* iq, const bf16* iw,
+                           float* wout, int full, int T, void* stream) {
+  if (T <= 0) return 0;
+  glm_q_post<<<T, 256, 0, (cudaStream_t)stream>>>(qb, ldb, rope, pos, qmla, iq, iw, wout, full, T);
   return ref_status();
 }

@@ -26,7 +26,7 @@ ROOT = HERE.parents[1]
 sys.path[:0] = [str(ROOT), str(ROOT / "kern-glm53_b200"), str(ROOT / "tests")]
 
 from glmkv import workload as W  # noqa: E402
-from layer_case import LayerCase, run_reference, to_host  # noqa: E402
+from layer_case import LayerCase, q_post_case, run_reference, to_host  # noqa: E402
 
 # (name, call config, call seed, case seed, kv dtype, full layer, zero tiles)
 SMALL = [
@@ -41,6 +41,7 @@ DIGEST = [
     ("cfg1_fp8_full", "cfg1", 3, 11, "fp8", True, 16),
 ]
 EXACT = ("pos", "ks", "ke", "klen", "row_seq", "zero", "ind", "tlen")
+Q_POST = [("q_post_full", 512, 41, True), ("q_post_shared", 512, 42, False)]  # (name, rows, seed, full)
 
 
 def small_call(seed):
@@ -93,6 +94,31 @@ def run_case(torch, spec):
     return case, to_host(d, torch)
 
 
+def q_post_outputs(torch, T, seed, full):
+    """glm_q_post of the reference on q_post_case(T, seed): qmla (tails only), iq, wout."""
+    from oracle import ref
+    c = q_post_case(T, seed)
+    dev = torch.device("cuda:0")
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    qb, rope, pos, iw = t(c["qb"].view(np.int16)), t(c["rope"].view(np.int16)), t(c["pos"]), t(c["iw"].view(np.int16))
+    qmla = torch.zeros(T * 64 * 576, dtype=torch.int16, device=dev)
+    iq = torch.zeros(T * 32 * 128, dtype=torch.uint8, device=dev)
+    wout = torch.zeros(T * 32, dtype=torch.float32, device=dev)
+    p = lambda x: x.data_ptr()
+    ref.q_post(p(qb), c["ldb"], p(rope), p(pos), p(qmla), p(iq) if full else None, p(iw) if full else None,
+               p(wout) if full else None, int(full), T)
+    torch.cuda.synchronize()
+    tails = qmla.cpu().numpy().view(np.uint16).reshape(T, 64, 576)[:, :, 512:]
+    return c, {"qmla_tails": tails, "iq": iq.cpu().numpy(), "wout": wout.cpu().numpy().view(np.uint32)}
+
+
+def q_post_input_digest(c):
+    h = hashlib.sha256()
+    for a in (c["qb"], c["rope"], c["pos"], c["iw"]):
+        h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=str(HERE))
@@ -118,6 +144,9 @@ def main():
             dg["kg_prefix"] = sha(res["kg"].reshape(-1, 128)[pr])
             dg["ksf_prefix"] = sha(res["ksf"][pr])
         digests[spec[0]] = dg
+    for name, T, seed, full in Q_POST:
+        c, res = q_post_outputs(torch, T, seed, full)
+        digests[name] = {"input_sha": q_post_input_digest(c), **{k: sha(v) for k, v in res.items()}}
     (out / "ref_digests.json").write_text(json.dumps(digests, indent=1, sort_keys=True) + "\n")
     print("golden vectors written to", out)
 

@@ -166,3 +166,18 @@ def to_host(d, torch):
             a = a.view(np.uint16)
         out[k] = a
     return out
+
+
+LDB = 64 * 256 + 32 * 128  # NB[True] (kern-glm53 scripts/gen.py:63)
+
+
+def q_post_case(T, seed, ldb=LDB):
+    """Inputs of glm_q_post: q_b's output [T, ldb] bf16 (scaled N(0, 1) rows), rope, positions, iw."""
+    rng = np.random.default_rng(seed)
+    qb = np.zeros((T, ldb), np.uint16)
+    qb[:, :LDB] = W.bf16_bits(rng.standard_normal((T, LDB), dtype=np.float32) * rng.uniform(0.1, 8, (T, 1)))
+    n_pos = 4096
+    return {"qb": qb, "rope": W.rope_table(n_pos), "pos": rng.integers(0, n_pos, T).astype(np.int32),
+            "iw": W.bf16_bits(rng.standard_normal((T, 32), dtype=np.float32)), "T": T, "ldb": ldb}
+
+

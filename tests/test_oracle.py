@@ -106,6 +106,27 @@ def test_ue8m0_and_quant_known_answer():
     assert np.all(h["qq"][:2048] == cpu.e4m3_from_f32(np.float32([256.0]))[0])
 
 
+def test_q_post_known_answer():
+    """cos 1 / sin 0 leaves q_pe as it is; an indexer head whose largest value is 448 has scale 1."""
+    T, ldb = 1, 64 * 256 + 32 * 128
+    qb = np.zeros((T, ldb), np.uint16)
+    qb[0, 192:256] = W.bf16_bits(np.arange(64, dtype=np.float32) - 32)          # head 0's q_pe
+    qb[0, 16384:16384 + 128] = W.bf16_bits(np.linspace(-448, 448, 128, dtype=np.float32))
+    rope = np.zeros((1, 64), np.uint16)
+    rope[0, :32] = W.bf16_bits(np.ones(32, np.float32))
+    qmla = np.zeros(64 * 576, np.uint16)
+    iq = np.zeros(32 * 128, np.uint8)
+    iw = W.bf16_bits(np.full(32, 2.0, np.float32))
+    wout = np.zeros(32, np.float32)
+    cpu.q_post(qb, ldb, rope, np.int32([0]), qmla, iq, iw, wout, 1, T)
+    assert_equal(qmla[512:576], qb[0, 192:256], "q_pe through an identity rope")
+    vals = np.linspace(-448, 448, 128, dtype=np.float32)
+    assert_equal(iq[:128], cpu.e4m3_from_f32(W.bf16_value(W.bf16_bits(vals))), "head 0 at scale 1")
+    assert wout[0] == np.float32(np.float32(np.float32(2.0 * 1.0) * np.float32(0.08838834764831845)) *
+                                 np.float32(0.17677669529663687))
+    assert np.all(wout[1:] == wout[1])  # all-zero heads: scale from eps 1e-4
+
+
 # ------------------------------------------------------------------------------------------ pinned to the reference
 
 def _small_case(name):
@@ -185,3 +206,28 @@ def test_oracle_matches_reference_digests(name):
     if "kg_prefix" in want:
         assert _sha(h["kg"].reshape(-1, 128)[pr]) == want["kg_prefix"], f"{name}: kg prefix rows"
         assert _sha(h["ksf"][pr]) == want["ksf_prefix"], f"{name}: ksf prefix rows"
+
+
+@pytest.mark.parametrize("name", ["q_post_full", "q_post_shared"])
+def test_oracle_q_post_matches_reference_digests(name):
+    path = GOLDEN / "ref_digests.json"
+    want = json.loads(path.read_text()) if path.exists() else {}
+    if name not in want:
+        pytest.skip("q_post golden vectors not generated yet (tests/golden/make_golden.py on a GPU)")
+    want = want[name]
+    import sys
+    sys.path.insert(0, str(GOLDEN))
+    import make_golden as MG
+    from layer_case import q_post_case
+
+    _, T, seed, full = {q[0]: q for q in MG.Q_POST}[name]
+    c = q_post_case(T, seed)
+    assert want["input_sha"] == MG.q_post_input_digest(c), "input generator drifted from the recorded vectors"
+    qmla = np.zeros(T * 64 * 576, np.uint16)
+    iq = np.zeros(T * 32 * 128, np.uint8)
+    wout = np.zeros(T * 32, np.float32)
+    cpu.q_post(c["qb"], c["ldb"], c["rope"], c["pos"], qmla, iq if full else None, c["iw"] if full else None,
+               wout if full else None, full, T)
+    assert _sha(qmla.reshape(T, 64, 576)[:, :, 512:]) == want["qmla_tails"]
+    assert _sha(iq) == want["iq"]
+    assert _sha(wout.view(np.uint32)) == want["wout"]
