@@ -85,13 +85,34 @@ __device__ __forceinline__ uint16_t fp8x2(float a, float b) {
   return __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
 }
 
-// The UE8M0 scale: 2^ceil(log2(max(amax, eps) / 448)) and its exponent byte (glm_glue.cu:68-74).
+// The UE8M0 scale of a block (glm_glue.cu:68-74): the exponent byte of the correctly rounded
+// q = max(amax, eps) / 448, plus one when q is not a power of two; the scale is that power of two.
+// Computed on the bits of x = max(amax, eps) without the division. With x = 2^e (1 + M / 2^23),
+// x / 448 = 2^(e - 9) (1 + M / 2^23) * 8 / 7, and (1 + M / 2^23) * 8 / 7 lies in [8/7, 2) for
+// M <= 0x600000 (exactly 2 at M = 0x600000, q = 2^(e - 8)) and in (2, 16/7) above it. The nearest
+// f32 to q never crosses those powers of two, because a quotient within half an ulp of one would need
+// x within 2^-24 of 7 * 2^k, and the only f32 there is 7 * 2^k itself. So the byte is
+// E - 8 + (M > 0x600000), E the biased exponent of x. x is a normal number (x >= eps >= 1e-10);
+// x = inf gives 255 as the quotient would. eps keeps NaN out (fmaxf drops it).
+__device__ __forceinline__ unsigned ue8m0_byte(float amax, float eps) {
+  const unsigned b = __float_as_uint(fmaxf(amax, eps));
+  const unsigned E = b >> 23, M = b & 0x7fffffu;
+  return E == 255u ? 255u : E - 8u + (M > 0x600000u ? 1u : 0u);
+}
 __device__ __forceinline__ float ue8m0(float amax, float eps, unsigned* e) {
+  *e = ue8m0_byte(amax, eps);
+  return __uint_as_float(*e << 23);
+}
+// The same byte through the division itself (the reference's form); identical results. The append's
+// q quant uses this one: measured faster there, where the division overlaps the reductions.
+__device__ __forceinline__ float ue8m0_div(float amax, float eps, unsigned* e) {
   const unsigned b = __float_as_uint(__fdiv_rn(fmaxf(amax, eps), 448.f));
-  unsigned x = (b >> 23) & 0xffu;
-  x += (b & 0x7fffffu) != 0;
-  *e = x;
-  return __uint_as_float(x << 23);
+  *e = ((b >> 23) & 0xffu) + ((b & 0x7fffffu) != 0 ? 1u : 0u);
+  return __uint_as_float(*e << 23);
+}
+// 1 / 2^(e - 127) exactly (the reciprocal of a UE8M0 scale): v * this rounds exactly as v / scale.
+__device__ __forceinline__ float ue8m0_inv(unsigned e) {
+  return e <= 253u ? __uint_as_float((254u - e) << 23) : (e == 254u ? __uint_as_float(0x00400000u) : 0.f);
 }
 
 // Two e4m3 bytes -> two bf16 of (value * sc): the f32 product rounded, then rounded to bf16

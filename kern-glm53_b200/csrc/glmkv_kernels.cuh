@@ -186,7 +186,7 @@ __device__ __forceinline__ void prep_row(const Row& row, const float* __restrict
     am[kb] = fmaxf(bf_lo(m), bf_hi(m));
   }
   unsigned e;
-  const float inv = __frcp_rn(ue8m0(max16_scatter(am, l), 1e-10f, &e));  // lane l: block kb = l >> 1
+  const float inv = __frcp_rn(ue8m0_div(max16_scatter(am, l), 1e-10f, &e));  // lane l: block kb = l >> 1
   u8* qrow = qq + (size_t)r * QL;
 #pragma unroll
   for (int kb = 0; kb < 16; ++kb) {
@@ -273,11 +273,11 @@ __device__ __forceinline__ void prep_row(const Row& row, const float* __restrict
   }
   const float amax = warp_max(fmaxf(fmaxf(fabsf(n[0]), fabsf(n[1])), fmaxf(fabsf(n[2]), fabsf(n[3]))));
   unsigned ex;
-  const float sc = ue8m0(amax, 1e-4f, &ex);
+  const float sc = ue8m0(amax, 1e-4f, &ex), isc = ue8m0_inv(ex);  // n * (1 / sc) rounds as n / sc
   u8* page = idx + (size_t)(s / PAGE) * IDX_PAGE;
   const int i = (int)(s % PAGE);
   *reinterpret_cast<uint32_t*>(page + i * ID + 4 * l) =
-      fp8x4(__fdiv_rn(n[0], sc), __fdiv_rn(n[1], sc), __fdiv_rn(n[2], sc), __fdiv_rn(n[3], sc));
+      fp8x4(__fmul_rn(n[0], isc), __fmul_rn(n[1], isc), __fmul_rn(n[2], isc), __fmul_rn(n[3], isc));
   if (l == 0) reinterpret_cast<float*>(page + PAGE * ID)[i] = sc;
 }
 
@@ -617,9 +617,11 @@ constexpr int QP_THREADS = 32 * QP_WARPS;
 //    instruction covers four heads;
 //  - on indexer layers, the indexer query: lane l holds dims 4l .. 4l + 3 of each of the 32 heads
 //    (the reference's layout), rope on dims 0..63, e4m3 of v / sc with the head's UE8M0 scale (eps
-//    1e-4), and the head weight ((iw * sc) * 128^-0.5) * 32^-0.5.
+//    1e-4), and the head weight ((iw * sc) * 128^-0.5) * 32^-0.5. Heads go eight at a time: one
+//    reduce-scatter leaves head (l >> 2) & 7's max in lane l, which derives that head's scale.
 // Every rope product is bf16 x bf16, exact in f32, so the rounding is the reference's whatever the
-// contraction. sc is a power of two, so v * (1 / sc) rounds exactly as v / sc.
+// contraction. sc is a power of two, so v * (1 / sc) rounds exactly as v / sc. All of the row's
+// q_pe loads and the first eight heads of the query are in flight before any arithmetic.
 template <bool FULL>
 __device__ __forceinline__ void q_post_row(const bf16* __restrict__ qb, int ldb, const bf16* __restrict__ rope, int p,
                                            bf16* __restrict__ qmla, u8* __restrict__ iq, const bf16* __restrict__ iw,
@@ -627,67 +629,80 @@ __device__ __forceinline__ void q_post_row(const bf16* __restrict__ qb, int ldb,
   const u8* row = reinterpret_cast<const u8*>(qb + (size_t)r * ldb);
   const unsigned* cs = reinterpret_cast<const unsigned*>(rope + (size_t)p * 2 * HALF);
   const int q = l & 7;
+  uint4 v[16];  // q_pe: pairs 4q .. 4q + 3 of heads 4k + (l >> 3)
+#pragma unroll
+  for (int k = 0; k < 16; ++k) v[k] = ld_stream_v4u(row + 2 * ((4 * k + (l >> 3)) * QHD + NOPE) + 16 * q);
+  uint2 g0[8];  // the indexer query's heads 0..7, dims 4l .. 4l + 3
+  if constexpr (FULL) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) g0[k] = ld_stream_v2(row + 2 * (HEADS * QHD + k * ID + 4 * l));
+  }
   // rope values of this lane's pairs 4q .. 4q + 3: cos at cs[4q ..], sin at cs[32 + 4q ..]
   const uint2 cw = __ldg(reinterpret_cast<const uint2*>(cs) + q), sw = __ldg(reinterpret_cast<const uint2*>(cs + 16) + q);
   const float c[4] = {bf_lo(cw.x), bf_hi(cw.x), bf_lo(cw.y), bf_hi(cw.y)};
   const float sn[4] = {bf_lo(sw.x), bf_hi(sw.x), bf_lo(sw.y), bf_hi(sw.y)};
   u8* out = reinterpret_cast<u8*>(qmla + (size_t)r * HEADS * MLA);
 #pragma unroll
-  for (int half = 0; half < 2; ++half) {  // eight 16-byte loads in flight at a time
-    uint4 v[8];
+  for (int k = 0; k < 16; ++k) {
+    const int h = 4 * k + (l >> 3);
+    const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+    uint32_t o[4];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int h = 4 * (8 * half + k) + (l >> 3);
-      v[k] = ld_stream_v4u(row + 2 * (h * QHD + NOPE) + 16 * q);
+    for (int i = 0; i < 4; ++i) {
+      const float x1 = bf_lo(w[i]), x2 = bf_hi(w[i]);
+      o[i] = pack_bf16x2(__fmaf_rn(x1, c[i], -__fmul_rn(x2, sn[i])), __fmaf_rn(x2, c[i], __fmul_rn(x1, sn[i])));
     }
+    *reinterpret_cast<uint4*>(out + 2 * (h * MLA + KVL) + 16 * q) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  if constexpr (FULL) {
+    // lane l < 16 ropes dims 4l .. 4l + 3 (pairs 2l, 2l + 1)
+    const unsigned c2 = l < 16 ? __ldg(cs + l) : 0u, s2 = l < 16 ? __ldg(cs + 16 + l) : 0u;
+    const float ca = bf_lo(c2), sa = bf_lo(s2), cb = bf_hi(c2), sb = bf_hi(s2);
+    uint2 cur[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int h = 4 * (8 * half + k) + (l >> 3);
-      const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-      uint32_t o[4];
+    for (int k = 0; k < 8; ++k) cur[k] = g0[k];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float x1 = bf_lo(w[i]), x2 = bf_hi(w[i]);
-        o[i] = pack_bf16x2(__fmaf_rn(x1, c[i], -__fmul_rn(x2, sn[i])), __fmaf_rn(x2, c[i], __fmul_rn(x1, sn[i])));
+    for (int g = 0; g < IH / 8; ++g) {
+      uint2 nxt[8];
+      if (g + 1 < IH / 8) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) nxt[k] = ld_stream_v2(row + 2 * (HEADS * QHD + (8 * (g + 1) + k) * ID + 4 * l));
       }
-      *reinterpret_cast<uint4*>(out + 2 * (h * MLA + KVL) + 16 * q) = make_uint4(o[0], o[1], o[2], o[3]);
+      float n[8][4], m8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        n[k][0] = bf_lo(cur[k].x), n[k][1] = bf_hi(cur[k].x), n[k][2] = bf_lo(cur[k].y), n[k][3] = bf_hi(cur[k].y);
+        if (l < 16) {
+          const float e0 = n[k][0], o0 = n[k][1], e1 = n[k][2], o1 = n[k][3];
+          n[k][0] = __fmaf_rn(e0, ca, -__fmul_rn(o0, sa));
+          n[k][1] = __fmaf_rn(o0, ca, __fmul_rn(e0, sa));
+          n[k][2] = __fmaf_rn(e1, cb, -__fmul_rn(o1, sb));
+          n[k][3] = __fmaf_rn(o1, cb, __fmul_rn(e1, sb));
+        }
+        m8[k] = fmaxf(fmaxf(fabsf(n[k][0]), fabsf(n[k][1])), fmaxf(fabsf(n[k][2]), fabsf(n[k][3])));
+      }
+      const unsigned e = ue8m0_byte(max8_scatter(m8, l), 1e-4f);  // lane l: head 8g + ((l >> 2) & 7)
+      const float inv = ue8m0_inv(e);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float iv = __shfl_sync(FULL, inv, 4 * k);
+        *reinterpret_cast<uint32_t*>(iq + ((size_t)r * IH + 8 * g + k) * ID + 4 * l) =
+            fp8x4(__fmul_rn(n[k][0], iv), __fmul_rn(n[k][1], iv), __fmul_rn(n[k][2], iv), __fmul_rn(n[k][3], iv));
+      }
+      if ((l & 3) == 0) {  // lane 4k: head 8g + k's weight
+        const int ih = 8 * g + (l >> 2);
+        float x = __bfloat162float(iw[(size_t)r * IH + ih]);
+        x = __fmul_rn(x, __uint_as_float(e << 23));
+        x = __fmul_rn(x, 0.08838834764831845f);
+        x = __fmul_rn(x, 0.17677669529663687f);
+        wout[(size_t)r * IH + ih] = x;
+      }
+      if (g + 1 < IH / 8) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) cur[k] = nxt[k];
+      }
     }
   }
-  if constexpr (!FULL) return;
-  // the indexer query: lane l < 16 ropes dims 4l .. 4l + 3 (pairs 2l, 2l + 1)
-  const unsigned c2 = l < 16 ? __ldg(cs + l) : 0u, s2 = l < 16 ? __ldg(cs + 16 + l) : 0u;
-  float mysc = 0.f;
-#pragma unroll
-  for (int g = 0; g < IH / 8; ++g) {
-    uint2 v[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = ld_stream_v2(row + 2 * (HEADS * QHD + (8 * g + k) * ID + 4 * l));
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int ih = 8 * g + k;
-      float n[4] = {bf_lo(v[k].x), bf_hi(v[k].x), bf_lo(v[k].y), bf_hi(v[k].y)};
-      if (l < 16) {
-        const float ca = bf_lo(c2), sa = bf_lo(s2), cb = bf_hi(c2), sb = bf_hi(s2);
-        const float e0 = n[0], o0 = n[1], e1 = n[2], o1 = n[3];
-        n[0] = __fmaf_rn(e0, ca, -__fmul_rn(o0, sa));
-        n[1] = __fmaf_rn(o0, ca, __fmul_rn(e0, sa));
-        n[2] = __fmaf_rn(e1, cb, -__fmul_rn(o1, sb));
-        n[3] = __fmaf_rn(o1, cb, __fmul_rn(e1, sb));
-      }
-      unsigned ex;
-      const float sc = ue8m0(warp_max(fmaxf(fmaxf(fabsf(n[0]), fabsf(n[1])), fmaxf(fabsf(n[2]), fabsf(n[3])))), 1e-4f,
-                             &ex);
-      const float inv = __frcp_rn(sc);
-      *reinterpret_cast<uint32_t*>(iq + ((size_t)r * IH + ih) * ID + 4 * l) =
-          fp8x4(__fmul_rn(n[0], inv), __fmul_rn(n[1], inv), __fmul_rn(n[2], inv), __fmul_rn(n[3], inv));
-      if (l == ih) mysc = sc;
-    }
-  }
-  float x = __bfloat162float(iw[(size_t)r * IH + l]);  // lane l: head l's weight
-  x = __fmul_rn(x, mysc);
-  x = __fmul_rn(x, 0.08838834764831845f);
-  x = __fmul_rn(x, 0.17677669529663687f);
-  wout[(size_t)r * IH + l] = x;
 }
 
 }  // namespace glmkv
@@ -696,7 +711,7 @@ __device__ __forceinline__ void q_post_row(const bf16* __restrict__ qb, int ldb,
 // (glm_glue.cu:301-351). qb [T, ldb] bf16: 64 heads of nope 192 | pe 64, then 32 indexer heads of 128
 // at column 16384. On a shared layer iq, iw and wout are null (gen.py:120-123).
 //   grid ceil(T / 8), block 256: a warp a row
-extern "C" __global__ void __launch_bounds__(glmkv::QP_THREADS, 3)
+extern "C" __global__ void __launch_bounds__(glmkv::QP_THREADS, 2)
     glm_q_post(const glmkv::bf16* __restrict__ qb, int ldb, const glmkv::bf16* __restrict__ rope,
                const int* __restrict__ pos, glmkv::bf16* __restrict__ qmla, glmkv::u8* __restrict__ iq,
                const glmkv::bf16* __restrict__ iw, float* __restrict__ wout, int full, int T) {
