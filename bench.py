@@ -262,7 +262,42 @@ def next_rows(torch, impl, T, dev, reps=10):
         nbytes = traffic.q_post(T, full)
         out["indexer_layer" if full else "shared_layer"] = {"us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1),
                                                             "algorithmic_bytes": nbytes}
-    return {"glm_q_post": {"rows": T, **out}}
+    rows = {"glm_q_post": {"rows": T, **out}}
+    del qb, qmla, iq, iw, wout
+    # the norm + quant glue of a layer: norm_in / norm_post (add_rms_quant) and quant_o (glm_quant)
+    H, K = 6144, 64 * 256
+    a_ = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+    res_ = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+    gam = (torch.rand(H, device=dev, generator=g) + 0.5).to(torch.bfloat16)
+    nrm = torch.empty_like(res_)
+    qh = torch.empty(T * H, dtype=torch.uint8, device=dev)
+    sfh = torch.empty(H // 512 * T * 4, dtype=torch.uint8, device=dev)
+    xo = torch.randn(T, K, device=dev, generator=g).to(torch.bfloat16)
+    qo = torch.empty(T * K, dtype=torch.uint8, device=dev)
+    sfo = torch.empty(K // 512 * T * 4, dtype=torch.uint8, device=dev)
+    if impl == "glmkv":
+        f_arq = lambda: glmkv.add_rms_quant(a_, res_, gam, nrm, qh, sfh, T, T)
+        f_q = lambda: glmkv.quant_o(xo, K, qo, sfo, T, K, T)
+    else:
+        from oracle import ref
+        p = lambda t: t.data_ptr()
+        f_arq = lambda: ref.add_rms_quant(p(a_), p(res_), p(gam), p(nrm), p(qh), p(sfh), T, T)
+        f_q = lambda: ref.quant(p(xo), K, p(qo), p(sfo), T, K, T)
+    for name, fn, nbytes in (("glm_add_rms_quant", f_arq, traffic.add_rms_quant(T)),
+                             ("glm_quant", f_q, traffic.quant(T, K))):
+        for _ in range(2):
+            fn()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(reps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        us = s.elapsed_time(e) / reps * 1e3
+        rows[name] = {"rows": T, "us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1), "algorithmic_bytes": nbytes}
+    rows["glm_quant"]["K"] = K
+    return rows
 
 
 # ------------------------------------------------------------------------------------------ CPU baseline

@@ -100,9 +100,24 @@ int glmkv_topk_slots(int32_t* ind, const int32_t* block_table, int max_pages, co
 int glmkv_q_post(const void* qb, int ldb, const void* rope, const int32_t* pos, void* qmla, void* iq, const void* iw,
                  float* wout, int full, int T, glmkv_stream_t stream);
 
+/* The residual add + RMSNorm + quant: res = bf16(a + res) written back (a NULL: res is already the
+ * stream), normed = bf16(bf16(res * rr) * gamma) with rr = rsqrt(sum(res^2) / 6144 + 1e-5), and normed
+ * quantized per 128 columns into q [T, 6144] e4m3 and sf (DeepGEMM-packed UE8M0 words
+ * [(6144 / 512)][sf_rows]). Rows are 6144 wide. normed, q (with sf) may be NULL.
+ * Replaces ops `add_rms_quant`, `rms_quant` (a NULL), `head_norm` (q, sf NULL) -> glm_add_rms_quant
+ * (kern-glm53 scripts/gen.py:156-158, 168-171; source/glm_glue.cu:127-162). Needs res and a 16-byte
+ * aligned, gamma and normed 8, q 4, sf_rows >= T when q is given. */
+int glmkv_add_rms_quant(const void* a, void* res, const void* gamma, void* normed, void* q, void* sf, int sf_rows,
+                        int T, glmkv_stream_t stream);
+
+/* x [T, K] bf16 (rows ldx apart) quantized per 128 columns into q [T, K] e4m3 and sf.
+ * Replaces op `quant_o` -> glm_quant (kern-glm53 scripts/gen.py:103-105; source/glm_glue.cu:164-175).
+ * Needs K % 128 == 0, ldx >= K, ldx % 8 == 0, x and q 16-byte aligned, sf 4, sf_rows >= T. */
+int glmkv_quant(const void* x, int ldx, void* q, void* sf, int sf_rows, int K, int T, glmkv_stream_t stream);
+
 /* The launch shape (grid x, block x, dynamic shared memory bytes) libglmkv uses for the kernel
  * `entry` ("glm_plan", "glm_mla_prep", "glm_mla_prep_fp8", "glm_idx_gather", "glm_kv_dequant",
- * "glm_topk_stream", "glm_topk_slots", "glm_q_post") on the current device for a call of T fresh rows: what a kern
+ * "glm_topk_stream", "glm_topk_slots", "glm_q_post", "glm_add_rms_quant") on the current device for a call of T fresh rows: what a kern
  * manifest's `impl.launches` entry for the cubin must use. The persistent page kernels depend on the
  * device's SM count only. No counterpart in the reference, whose shapes are fixed in its manifest
  * generator (kern-glm53 scripts/gen.py:95-135, 172-177). */

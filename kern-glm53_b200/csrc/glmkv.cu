@@ -27,6 +27,7 @@ struct DeviceInfo {
   int dq_ctas = 0;    // resident dequant CTAs an SM
   int ga_ctas = 0;    // resident gather CTAs an SM
   int prep_ctas = 0;  // resident append CTAs an SM
+  int arq_ctas = 0;   // resident add_rms_quant CTAs an SM
 };
 
 std::once_flag g_once[MAX_DEVICES];
@@ -54,7 +55,11 @@ const DeviceInfo* device_info() {
       ok = ok && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM) == cudaSuccess;
     ok = ok && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.prep_ctas, glm_mla_prep_fp8, PREP_THREADS,
                                                              PREP_SMEM) == cudaSuccess;
-    if (!ok || d.sms <= 0 || d.dq_ctas <= 0 || d.ga_ctas <= 0 || d.prep_ctas <= 0) {
+    ok = ok && cudaFuncSetAttribute(glm_add_rms_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, ARQ_SMEM) ==
+                   cudaSuccess;
+    ok = ok && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.arq_ctas, glm_add_rms_quant, ARQ_THREADS, ARQ_SMEM) ==
+                   cudaSuccess;
+    if (!ok || d.sms <= 0 || d.dq_ctas <= 0 || d.ga_ctas <= 0 || d.prep_ctas <= 0 || d.arq_ctas <= 0) {
       d.status = GLMKV_ERR_DEVICE;
       cudaGetLastError();
     }
@@ -192,11 +197,42 @@ GLMKV_API int glmkv_q_post(const void* qb, int ldb, const void* rope, const int3
                 (const bf16*)rope, pos, (bf16*)qmla, (u8*)iq, (const bf16*)iw, wout, full, T);
 }
 
+GLMKV_API int glmkv_add_rms_quant(const void* a, void* res, const void* gamma, void* normed, void* q, void* sf,
+                                  int sf_rows, int T, glmkv_stream_t stream) {
+  if (T < 0) return GLMKV_ERR_ARG;
+  if (T == 0) return GLMKV_OK;
+  if (!res || !gamma || (q && (!sf || sf_rows < T))) return GLMKV_ERR_ARG;
+  if (!aligned(res, 16) || (a && !aligned(a, 16)) || !aligned(gamma, 8) || (normed && !aligned(normed, 8)) ||
+      (q && !aligned(q, 4)))
+    return GLMKV_ERR_ALIGN;
+  const DeviceInfo* d = device_info();
+  if (!d) return GLMKV_ERR_DEVICE;
+  return launch(glm_add_rms_quant, std::min(d->sms * d->arq_ctas, T), ARQ_THREADS, ARQ_SMEM, stream, (const bf16*)a,
+                (bf16*)res, (const bf16*)gamma, (bf16*)normed, (u8*)q, (u8*)sf, sf_rows, T);
+}
+
+GLMKV_API int glmkv_quant(const void* x, int ldx, void* q, void* sf, int sf_rows, int K, int T, glmkv_stream_t stream) {
+  if (T < 0 || K < 0) return GLMKV_ERR_ARG;
+  if (T == 0 || K == 0) return GLMKV_OK;
+  if (!x || !q || !sf || K % 128 || ldx < K || sf_rows < T) return GLMKV_ERR_ARG;
+  if (ldx % 8 || !aligned(x, 16) || !aligned(q, 16) || !aligned(sf, 4)) return GLMKV_ERR_ALIGN;
+  const long long warps = (long long)T * ((K / 128 + 3) / 4);
+  const long long grid = (warps + QT_THREADS / 32 - 1) / (QT_THREADS / 32);
+  if (grid > 0x7fffffffLL) return GLMKV_ERR_ARG;
+  return launch(glm_quant, (int)grid, QT_THREADS, 0, stream, (const bf16*)x, ldx, (u8*)q, (u8*)sf, sf_rows, K, T);
+}
+
 GLMKV_API int glmkv_launch_shape(const char* entry, int T, int* grid, int* block, int* smem_bytes) {
   if (!entry || !grid || !block || !smem_bytes || T < 0) return GLMKV_ERR_ARG;
   const auto is = [entry](const char* s) { return strcmp(entry, s) == 0; };
   if (is("glm_plan")) {
     *grid = (T + PLAN_THREADS - 1) / PLAN_THREADS, *block = PLAN_THREADS, *smem_bytes = 0;
+  } else if (is("glm_quant")) {
+    return GLMKV_ERR_ARG;  // its grid depends on K too: ceil(T * ceil(K / 512) / 8), block 256
+  } else if (is("glm_add_rms_quant")) {
+    const DeviceInfo* d = device_info();
+    if (!d) return GLMKV_ERR_DEVICE;
+    *grid = std::min(d->sms * d->arq_ctas, std::max(T, 1)), *block = ARQ_THREADS, *smem_bytes = ARQ_SMEM;
   } else if (is("glm_q_post")) {
     *grid = (T + QP_WARPS - 1) / QP_WARPS, *block = QP_THREADS, *smem_bytes = 0;
   } else if (is("glm_topk_stream") || is("glm_topk_slots")) {

@@ -726,6 +726,179 @@ extern "C" __global__ void __launch_bounds__(glmkv::QP_THREADS, 2)
     q_post_row<false>(qb, ldb, rope, pos[r], qmla, iq, iw, wout, r, threadIdx.x & 31);
 }
 
+// ================================================================================================ norm + quant glue
+
+namespace glmkv {
+
+constexpr int HID = 6144;                 // the residual stream's width
+constexpr int ARQ_THREADS = 256;          // the reference's thread (w, l) layout, kept for its sums
+constexpr int ARQ_ROW = HID * 2;          // 12288 B
+constexpr int ARQ_STAGES = 2;
+constexpr int ARQ_SMEM = ARQ_STAGES * 2 * ARQ_ROW;  // res and a rows, two stages: 49152 B
+constexpr int QT_THREADS = 256;
+
+// max(|.|) of the eight bf16 values in a uint4, as f32
+__device__ __forceinline__ float absmax8_bf16(uint4 v) {
+  return absmax_bf16x2(absmax2_bf16x2(absmax2_bf16x2(v.x, v.y), absmax2_bf16x2(v.z, v.w)));
+}
+
+// One 128-column block held four values a lane by a whole warp, quantized (glm_glue.cu:86-92):
+// amax over the warp, UE8M0 scale (eps 1e-10), e4m3 of y * (1 / scale); lane 0 writes the byte.
+__device__ __forceinline__ void quant_warp4(const float (&y)[4], u8* __restrict__ q, u8* __restrict__ sf, int sf_rows,
+                                            int r, int kb, int l) {
+  const float amax = warp_max(fmaxf(fmaxf(fabsf(y[0]), fabsf(y[1])), fmaxf(fabsf(y[2]), fabsf(y[3]))));
+  const unsigned e = ue8m0_byte(amax, 1e-10f);
+  const float inv = ue8m0_inv(e);
+  *reinterpret_cast<uint32_t*>(q) = fp8x4(__fmul_rn(y[0], inv), __fmul_rn(y[1], inv), __fmul_rn(y[2], inv),
+                                          __fmul_rn(y[3], inv));
+  if (l == 0) sf[((size_t)(kb >> 2) * sf_rows + r) * 4 + (kb & 3)] = (u8)e;
+}
+
+}  // namespace glmkv
+
+// res = bf16(a + res) (a null: res is already the stream), written back; normed = bf16(bf16(res * rr)
+// * gamma) with rr = rsqrt(block_sum(res^2) / 6144 + 1e-5); normed quantized per 128 columns into q /
+// sf when q is given (glm_glue.cu:127-162). normed, q, sf may be null (gen.py:156-171).
+// A persistent CTA of 256 threads takes rows b, b + G, ...: thread (w, l) holds the reference's
+// columns (6w + i) * 128 + 4l + j, so the sum is built in its order. The next row's res (and a) are
+// bulk-copied (TMA) into the CTA's other stage while this row is worked on.
+//   persistent: grid = SMs x resident CTAs, block 256, dynamic smem ARQ_SMEM (49,152 B)
+extern "C" __global__ void __launch_bounds__(glmkv::ARQ_THREADS, 3)
+    glm_add_rms_quant(const glmkv::bf16* __restrict__ a, glmkv::bf16* __restrict__ res,
+                      const glmkv::bf16* __restrict__ gamma, glmkv::bf16* __restrict__ normed,
+                      glmkv::u8* __restrict__ q, glmkv::u8* __restrict__ sf, int sf_rows, int T) {
+  using namespace glmkv;
+  extern __shared__ __align__(128) u8 smem[];
+  __shared__ __align__(8) unsigned long long full[ARQ_STAGES];
+  __shared__ float sm[8];
+  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+  if (tid == 0) {
+#pragma unroll
+    for (int st = 0; st < ARQ_STAGES; ++st) mbar_init(smem_u32(&full[st]), 1);
+    mbar_init_fence();
+  }
+  pdl_trigger();  // a persistent grid: all of its CTAs are resident
+  pdl_wait();
+  __syncthreads();
+  int r = blockIdx.x;
+  if (r >= T) return;
+  const bool has_a = a != nullptr;
+  const uint32_t bytes = has_a ? 2 * ARQ_ROW : ARQ_ROW;
+  auto issue = [&](int st, int row) {
+    const uint32_t bar = smem_u32(&full[st]);
+    u8* dst = smem + (size_t)st * 2 * ARQ_ROW;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_arrive_expect_tx(bar, bytes);
+    tma_load_1d(smem_u32(dst), res + (size_t)row * HID, ARQ_ROW, bar);
+    if (has_a) tma_load_1d(smem_u32(dst + ARQ_ROW), a + (size_t)row * HID, ARQ_ROW, bar);
+  };
+  uint2 gw[6];  // gamma of this thread's columns
+#pragma unroll
+  for (int i = 0; i < 6; ++i) gw[i] = __ldg(reinterpret_cast<const uint2*>(gamma + (w * 6 + i) * 128 + l * 4));
+  if (tid == 0) issue(0, r);
+  for (int k = 0; r < T; ++k, r += gridDim.x) {
+    const int st = k & 1, rn = r + gridDim.x;
+    if (rn < T && tid == 0) issue(st ^ 1, rn);  // that stage's row is done: block_sum synced past it
+    const bool ok = mbar_wait_bounded(smem_u32(&full[st]), (uint32_t)((k >> 1) & 1), WAIT_LIMIT_NS);
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) {
+        atomicOr(&g_fault, FAULT_WAIT_TIMEOUT);
+        if (rn < T) mbar_wait_bounded(smem_u32(&full[st ^ 1]), (uint32_t)(((k + 1) >> 1) & 1), WAIT_LIMIT_NS);
+      }
+      return;
+    }
+    const u8* srow = smem + (size_t)st * 2 * ARQ_ROW;
+    bf16* row = res + (size_t)r * HID;
+    float v[6][4], ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+      const int c = (w * 6 + i) * 128 + l * 4;
+      const uint2 rv = *reinterpret_cast<const uint2*>(srow + 2 * c);
+      v[i][0] = bf_lo(rv.x), v[i][1] = bf_hi(rv.x), v[i][2] = bf_lo(rv.y), v[i][3] = bf_hi(rv.y);
+      if (has_a) {
+        const uint2 av = *reinterpret_cast<const uint2*>(srow + ARQ_ROW + 2 * c);
+        v[i][0] = rnd(__fadd_rn(v[i][0], bf_lo(av.x)));
+        v[i][1] = rnd(__fadd_rn(v[i][1], bf_hi(av.x)));
+        v[i][2] = rnd(__fadd_rn(v[i][2], bf_lo(av.y)));
+        v[i][3] = rnd(__fadd_rn(v[i][3], bf_hi(av.y)));
+        *reinterpret_cast<uint2*>(row + c) = make_uint2(pack_bf16x2(v[i][0], v[i][1]), pack_bf16x2(v[i][2], v[i][3]));
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ss = __fmaf_rn(v[i][j], v[i][j], ss);  // squares of bf16 values: exact
+    }
+    // the reference's block_sum (glm_glue.cu:57-65): warp butterflies, then the eight warp totals
+    ss = warp_sum(ss);
+    __syncthreads();
+    if (l == 0) sm[w] = ss;
+    __syncthreads();
+    const float tot = warp_sum(l < 8 ? sm[l] : 0.f);
+    const float rr = rsqrtf(__fadd_rn(__fdiv_rn(tot, (float)HID), EPS));
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+      const int kb = w * 6 + i, c = kb * 128 + l * 4;
+      const float g[4] = {bf_lo(gw[i].x), bf_hi(gw[i].x), bf_lo(gw[i].y), bf_hi(gw[i].y)};
+      float y[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) y[j] = rnd(__fmul_rn(rnd(__fmul_rn(v[i][j], rr)), g[j]));
+      if (normed != nullptr)
+        *reinterpret_cast<uint2*>(normed + (size_t)r * HID + c) = make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
+      if (q != nullptr) quant_warp4(y, q + (size_t)r * HID + c, sf, sf_rows, r, kb, l);
+    }
+  }
+}
+
+// x [T, K] bf16 (rows ldx apart) quantized per 128 columns into q [T, K] e4m3 and DeepGEMM's packed
+// UE8M0 words [(K / 512)][sf_rows] (glm_glue.cu:164-175). A warp takes four consecutive blocks of a
+// row; lane l holds 16 values of block l >> 3 (two 16-byte loads), the block's amax is three
+// shuffles, and lane 0 writes the four scale bytes as one word.
+//   grid ceil(T * ceil(K / 512) / 8), block 256
+extern "C" __global__ void __launch_bounds__(glmkv::QT_THREADS)
+    glm_quant(const glmkv::bf16* __restrict__ x, int ldx, glmkv::u8* __restrict__ q, glmkv::u8* __restrict__ sf,
+              int sf_rows, int K, int T) {
+  using namespace glmkv;
+  pdl_trigger();
+  pdl_wait();
+  const int nb = K >> 7, ng = (nb + 3) >> 2;
+  const long long gwarp = ((long long)blockIdx.x * QT_THREADS + threadIdx.x) >> 5;
+  if (gwarp >= (long long)T * ng) return;
+  const int r = (int)(gwarp / ng), m = (int)(gwarp % ng), l = threadIdx.x & 31;
+  const int kb = 4 * m + (l >> 3);
+  const bool live = kb < nb;
+  const int col = kb * 128 + 16 * (l & 7);
+  uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
+  if (live) {
+    const u8* src = reinterpret_cast<const u8*>(x + (size_t)r * ldx + col);
+    v0 = ld_stream_v4u(src);
+    v1 = ld_stream_v4u(src + 16);
+  }
+  float amax = fmaxf(absmax8_bf16(v0), absmax8_bf16(v1));
+  amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, 4));
+  amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, 2));
+  amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, 1));
+  const unsigned e = ue8m0_byte(amax, 1e-10f);
+  const float inv = ue8m0_inv(e);
+  const float2 i2 = make_float2(inv, inv);
+  const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 p0 = mul2(unpack2(w[2 * i]), i2), p1 = mul2(unpack2(w[2 * i + 1]), i2);
+    o[i] = fp8x4(p0.x, p0.y, p1.x, p1.y);
+  }
+  if (live) *reinterpret_cast<uint4*>(q + (size_t)r * K + col) = make_uint4(o[0], o[1], o[2], o[3]);
+  const unsigned e1 = __shfl_sync(FULL, e, 8), e2 = __shfl_sync(FULL, e, 16), e3 = __shfl_sync(FULL, e, 24);
+  if (l == 0) {
+    u8* word = sf + ((size_t)m * sf_rows + r) * 4;
+    if (4 * m + 3 < nb) {
+      *reinterpret_cast<unsigned*>(word) = e | (e1 << 8) | (e2 << 16) | (e3 << 24);
+    } else {  // the row's last blocks: byte stores for the ones that exist
+      word[0] = (u8)e;
+      if (4 * m + 1 < nb) word[1] = (u8)e1;
+      if (4 * m + 2 < nb) word[2] = (u8)e2;
+    }
+  }
+}
+
 // Self-test of the bounded wait every pipeline uses: one thread waits on an mbarrier that nothing
 // ever arrives on, gives up after `limit_ns`, sets FAULT_WAIT_TIMEOUT and returns. No counterpart
 // in the reference.

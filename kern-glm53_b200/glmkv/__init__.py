@@ -6,8 +6,9 @@ dequant, the top-k row plans). The kernels are CUDA in ``libglmkv.so`` (C ABI: `
 this package binds them with ctypes and uses PyTorch only to own device memory.
 """
 from ._lib import CUBIN_PATH, LIB_PATH, GlmKvError, fault_flags, launch_shape, lib, strerror
-from .ops import (idx_gather, kv_dequant, mla_prep_full, mla_prep_shared, plan, q_post_full, q_post_shared, topk_slots,
-                  topk_stream)
+from .ops import (add_rms_quant, head_norm, idx_gather, kv_dequant, mla_prep_full, mla_prep_shared, plan, q_post_full,
+                  q_post_shared, quant_o, rms_quant, topk_slots, topk_stream)
 
 __all__ = ["CUBIN_PATH", "LIB_PATH", "GlmKvError", "fault_flags", "launch_shape", "lib", "strerror", "plan", "mla_prep_full",
-           "mla_prep_shared", "idx_gather", "kv_dequant", "topk_stream", "topk_slots", "q_post_full", "q_post_shared"]
+           "mla_prep_shared", "idx_gather", "kv_dequant", "topk_stream", "topk_slots", "q_post_full", "q_post_shared",
+           "add_rms_quant", "rms_quant", "head_norm", "quant_o"]

@@ -20,6 +20,10 @@ by the op's scalars, exactly in the manifest's parameter order, and enqueues one
     q_post_full      qb, ldb, rope, pos, qmla, iq, iw, wout, full, T       glm_q_post
                                                             (117-119)
     q_post_shared    the same without iq, iw, wout (nulled, 120-123)       glm_q_post
+    add_rms_quant    a, res, gamma, normed, q, sf, sf_rows, T (168-170)    glm_add_rms_quant
+    rms_quant        the same without a (nulled, 171)                      glm_add_rms_quant
+    head_norm        the same without q, sf (nulled, 156-158)              glm_add_rms_quant
+    quant_o          x, ldx, q, sf, sf_rows, K, T         (103-105)        glm_quant
 
 Errors (null or misaligned buffers, sizes out of range, a failed launch) raise ``GlmKvError``.
 """
@@ -120,3 +124,26 @@ def q_post_shared(qb, ldb, rope, pos, qmla, full, T, stream=None):
     """The q_pe rope of a shared layer (op `q_post_shared`, iq / iw / wout null)."""
     _lib.call("glmkv_q_post", _ptr(qb, "bf16", "qb"), int(ldb), _ptr(rope, "bf16", "rope"), _ptr(pos, "i32", "pos"),
               _ptr(qmla, "bf16", "qmla"), None, None, None, int(full), int(T), _stream(stream))
+
+
+def add_rms_quant(a, res, gamma, normed, q, sf, sf_rows, T, stream=None):
+    """res = bf16(a + res); normed = RMSNorm(res) * gamma; e4m3 per 128 columns (op `add_rms_quant`)."""
+    _lib.call("glmkv_add_rms_quant", _ptr(a, "bf16", "a"), _ptr(res, "bf16", "res"), _ptr(gamma, "bf16", "gamma"),
+              _ptr(normed, "bf16", "normed"), _ptr(q, "u8", "q"), _ptr(sf, "u8", "sf"), int(sf_rows), int(T),
+              _stream(stream))
+
+
+def rms_quant(res, gamma, normed, q, sf, sf_rows, T, stream=None):
+    """The first layer's norm: res is already the stream (op `rms_quant`, a null)."""
+    add_rms_quant(None, res, gamma, normed, q, sf, sf_rows, T, stream)
+
+
+def head_norm(a, res, gamma, normed, sf_rows, T, stream=None):
+    """The final norm of each sequence's last row, no quant (op `head_norm`, q and sf null)."""
+    add_rms_quant(a, res, gamma, normed, None, None, sf_rows, T, stream)
+
+
+def quant_o(x, ldx, q, sf, sf_rows, K, T, stream=None):
+    """x [T, K] e4m3 per 128 columns with packed UE8M0 scales (op `quant_o`)."""
+    _lib.call("glmkv_quant", _ptr(x, "bf16", "x"), int(ldx), _ptr(q, "u8", "q"), _ptr(sf, "u8", "sf"), int(sf_rows),
+              int(K), int(T), _stream(stream))

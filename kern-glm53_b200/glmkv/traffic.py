@@ -19,6 +19,10 @@ The next rows, around the path:
     q_post, indexer layer   fresh row      8192 q_pe + 8192 index query  8192 qmla tails + 4096    28996
                                            + 128 rope + 4 + 64 iw        iq + 128 wout
     q_post, shared layer    fresh row      8192 + 128 + 4                8192                      16516
+    add_rms_quant           row            12288 a + 12288 res           12288 res + 12288 normed  55344
+                                                                         + 6144 q + 48 sf
+    rms_quant (no a)        row            12288 res                     12288 + 6144 + 48         30768
+    quant (K columns)       row            2K                            K + K / 128               3K + K/128
 """
 QL, KVL, ROPE, ID, TOPK = 2048, 512, 64, 128, 2048
 
@@ -58,3 +62,14 @@ def layer(T, ctx, full, kv_dtype="fp8"):
 
 def q_post(T, full=True):
     return (28996 if full else 16516) * T
+
+
+def add_rms_quant(T, with_a=True, normed=True, quant=True):
+    H = 6144
+    read = 2 * H * (2 if with_a else 1)
+    write = (2 * H if with_a else 0) + (2 * H if normed else 0) + ((H + H // 128) if quant else 0)
+    return (read + write) * T
+
+
+def quant(T, K):
+    return (3 * K + K // 128) * T

@@ -25,6 +25,8 @@ def lib():
         _lib.orc_topk_stream.argtypes = [P, P, P, P, I]
         _lib.orc_topk_slots.argtypes = [P, P, I, P, P, P, I]
         _lib.orc_q_post.argtypes = [P, I, P, P, P, P, P, P, I, I]
+        _lib.orc_add_rms_quant.argtypes = [P, P, P, P, P, P, I, I]
+        _lib.orc_quant.argtypes = [P, I, P, P, I, I, I]
         _lib.orc_bf16_from_f32.argtypes = [P, P, ctypes.c_long]
         _lib.orc_e4m3_from_f32.argtypes = [P, P, ctypes.c_long]
         _lib.orc_f32_from_e4m3.argtypes = [P, P, ctypes.c_long]
@@ -111,3 +113,12 @@ def f32_from_e4m3(x):
 def q_post(qb, ldb, rope, pos, qmla, iq, iw, wout, full, T):
     lib().orc_q_post(_p(qb, np.uint16), ldb, _p(rope, np.uint16), _p(pos, np.int32), _p(qmla, np.uint16),
                      _p(iq, np.uint8), _p(iw, np.uint16), _p(wout, np.float32), int(bool(full)), T)
+
+
+def add_rms_quant(a, res, gamma, normed, q, sf, sf_rows, T):
+    lib().orc_add_rms_quant(_p(a, np.uint16), _p(res, np.uint16), _p(gamma, np.uint16), _p(normed, np.uint16),
+                            _p(q, np.uint8), _p(sf, np.uint8), sf_rows, T)
+
+
+def quant(x, ldx, q, sf, sf_rows, K, T):
+    lib().orc_quant(_p(x, np.uint16), ldx, _p(q, np.uint8), _p(sf, np.uint8), sf_rows, K, T)

@@ -427,6 +427,71 @@ void orc_q_post(const uint16_t* qb, int ldb, const uint16_t* rope, const int32_t
   }
 }
 
+/* ---------------------------------------------------------------- glm_add_rms_quant, glm_quant */
+
+#define HID 6144
+
+/* Four values of a 128-column block quantized (glm_glue.cu:85-92): amax of the block, UE8M0 scale
+ * with eps 1e-10, e4m3 of v * (1 / scale); the exponent byte into DeepGEMM's packed layout. */
+static void quant_block(const float* y, uint8_t* q, uint8_t* sf, int sf_rows, int r, int kb) {
+  float amax = 0.f;
+  for (int c = 0; c < 128; ++c) amax = fmaxf(amax, fabsf(y[c]));
+  uint8_t e;
+  const float inv = 1.0f / ue8m0(amax, 1e-10f, &e);
+  for (int c = 0; c < 128; ++c) q[c] = f_e4m3(y[c] * inv);
+  sf[((size_t)(kb >> 2) * sf_rows + r) * 4 + (kb & 3)] = e;
+}
+
+/* glm_glue.cu:127-162: res = bf16(a + res) when a is given (written back), then
+ * normed = bf16(bf16(res * rr) * gamma), rr = rsqrt(block_sum(res^2) / 6144 + 1e-5), quantized per 128
+ * columns when q is given. Thread (w, l) of the reference's 256 holds columns (6w + i) * 128 + 4l + j. */
+void orc_add_rms_quant(const uint16_t* a, uint16_t* res, const uint16_t* gamma, uint16_t* normed, uint8_t* q,
+                       uint8_t* sf, int sf_rows, int T) {
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < T; ++r) {
+    uint16_t* row = res + (size_t)r * HID;
+    float v[HID], part[256];
+    for (int c = 0; c < HID; ++c) {
+      v[c] = bf16_f(row[c]);
+      if (a) {
+        v[c] = rnd(v[c] + bf16_f(a[(size_t)r * HID + c]));
+        row[c] = f_bf16(v[c]);
+      }
+    }
+    for (int t = 0; t < 256; ++t) {
+      const int w = t >> 5, l = t & 31;
+      float ss = 0.f;
+      for (int i = 0; i < 6; ++i)
+        for (int j = 0; j < 4; ++j) {
+          const float x = v[(w * 6 + i) * 128 + l * 4 + j];
+          ss = ss + x * x;
+        }
+      part[t] = ss;
+    }
+    const float rr = rsqrt_cr(block_sum256(part) / (float)HID + EPS);
+    float y[HID];
+    for (int c = 0; c < HID; ++c) {
+      float t = v[c] * rr;
+      t = rnd(t) * bf16_f(gamma[c]);
+      y[c] = rnd(t);
+      if (normed) normed[(size_t)r * HID + c] = f_bf16(y[c]);
+    }
+    if (q)
+      for (int kb = 0; kb < HID / 128; ++kb) quant_block(y + kb * 128, q + (size_t)r * HID + kb * 128, sf, sf_rows, r, kb);
+  }
+}
+
+/* glm_glue.cu:164-175: x [T, K] (rows ldx apart) quantized per 128 columns into q [T, K] and sf. */
+void orc_quant(const uint16_t* x, int ldx, uint8_t* q, uint8_t* sf, int sf_rows, int K, int T) {
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < T; ++r)
+    for (int kb = 0; kb < (K >> 7); ++kb) {
+      float y[128];
+      for (int c = 0; c < 128; ++c) y[c] = bf16_f(x[(size_t)r * ldx + kb * 128 + c]);
+      quant_block(y, q + (size_t)r * K + kb * 128, sf, sf_rows, r, kb);
+    }
+}
+
 /* ---------------------------------------------------------------- helpers exported for tests */
 
 void orc_bf16_from_f32(const float* x, uint16_t* y, long n) {

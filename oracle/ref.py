@@ -34,6 +34,8 @@ def lib():
         _lib.ref_glm_topk_stream.argtypes = [P, P, P, P, I, P]
         _lib.ref_glm_topk_slots.argtypes = [P, P, I, P, P, P, I, P]
         _lib.ref_glm_q_post.argtypes = [P, I, P, P, P, P, P, P, I, I, P]
+        _lib.ref_glm_add_rms_quant.argtypes = [P, P, P, P, P, P, I, I, P]
+        _lib.ref_glm_quant.argtypes = [P, I, P, P, I, I, I, P]
     return _lib
 
 
@@ -70,3 +72,11 @@ def topk_slots(ind, block_table, max_pages, row_seq, klen, tlen, T, stream=0):
 
 def q_post(qb, ldb, rope, pos, qmla, iq, iw, wout, full, T, stream=0):
     _check(lib().ref_glm_q_post(qb, ldb, rope, pos, qmla, iq, iw, wout, int(bool(full)), T, stream), "glm_q_post")
+
+
+def add_rms_quant(a, res, gamma, normed, q, sf, sf_rows, T, stream=0):
+    _check(lib().ref_glm_add_rms_quant(a, res, gamma, normed, q, sf, sf_rows, T, stream), "glm_add_rms_quant")
+
+
+def quant(x, ldx, q, sf, sf_rows, K, T, stream=0):
+    _check(lib().ref_glm_quant(x, ldx, q, sf, sf_rows, K, T, stream), "glm_quant")

@@ -13,6 +13,8 @@
 //   glm_topk_stream    grid T,             block 256
 //   glm_topk_slots     grid T,             block 256
 //   glm_q_post         grid T,             block 256 (gen.py:117-123)
+//   glm_add_rms_quant  grid T,             block 256 (gen.py:168-171)
+//   glm_quant          grid ceil(T * K / 1024), block 256 (gen.py:103-105)
 // `ctx` is the manifest's launch variable (the sum of seq_lens); the caller passes it.
 #include <cuda_runtime.h>
 
@@ -78,5 +80,19 @@ REF_API int ref_glm_q_post(const bf16* qb, int ldb, const bf16* rope, const int*
                            float* wout, int full, int T, void* stream) {
   if (T <= 0) return 0;
   glm_q_post<<<T, 256, 0, (cudaStream_t)stream>>>(qb, ldb, rope, pos, qmla, iq, iw, wout, full, T);
+  return ref_status();
+}
+
+REF_API int ref_glm_add_rms_quant(const bf16* a, bf16* res, const bf16* gamma, bf16* normed, u8* q, u8* sf, int sf_rows,
+                                  int T, void* stream) {
+  if (T <= 0) return 0;
+  glm_add_rms_quant<<<T, 256, 0, (cudaStream_t)stream>>>(a, res, gamma, normed, q, sf, sf_rows, T);
+  return ref_status();
+}
+
+REF_API int ref_glm_quant(const bf16* x, int ldx, u8* q, u8* sf, int sf_rows, int K, int T, void* stream) {
+  const long long warps = (long long)T * (K >> 7);
+  if (warps <= 0) return 0;
+  glm_quant<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(x, ldx, q, sf, sf_rows, K, T);
   return ref_status();
 }

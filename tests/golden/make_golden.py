@@ -26,7 +26,7 @@ ROOT = HERE.parents[1]
 sys.path[:0] = [str(ROOT), str(ROOT / "kern-glm53_b200"), str(ROOT / "tests")]
 
 from glmkv import workload as W  # noqa: E402
-from layer_case import LayerCase, q_post_case, run_reference, to_host  # noqa: E402
+from layer_case import LayerCase, norm_case, q_post_case, quant_case, run_reference, to_host  # noqa: E402
 
 # (name, call config, call seed, case seed, kv dtype, full layer, zero tiles)
 SMALL = [
@@ -42,6 +42,8 @@ DIGEST = [
 ]
 EXACT = ("pos", "ks", "ke", "klen", "row_seq", "zero", "ind", "tlen")
 Q_POST = [("q_post_full", 512, 41, True), ("q_post_shared", 512, 42, False)]  # (name, rows, seed, full)
+NORM_SMALL = [("norm_add", 8, 51, True), ("norm_noadd", 8, 52, False)]  # (name, rows, seed, with a)
+QUANT = [("quant_640", 37, 640, 648), ("quant_16384", 512, 16384, 16384)]  # (name, rows, K, ldx)
 
 
 def small_call(seed):
@@ -119,6 +121,35 @@ def q_post_input_digest(c):
     return h.hexdigest()
 
 
+def norm_outputs(torch, T, seed, with_a):
+    """glm_add_rms_quant of the reference on norm_case(T, seed): res after the add, normed, q, sf."""
+    from oracle import ref
+    a, res, gamma = norm_case(T, seed, with_a)
+    dev = torch.device("cuda:0")
+    t = lambda x: None if x is None else torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).to(dev)
+    da, dres, dg = t(a), t(res), t(gamma)
+    normed = torch.zeros(T * 6144, dtype=torch.int16, device=dev)
+    q = torch.zeros(T * 6144, dtype=torch.uint8, device=dev)
+    sf = torch.zeros(12 * T * 4, dtype=torch.uint8, device=dev)
+    p = lambda x: None if x is None else x.data_ptr()
+    ref.add_rms_quant(p(da), p(dres), p(dg), p(normed), p(q), p(sf), T, T)
+    torch.cuda.synchronize()
+    return {"res": dres.cpu().numpy().view(np.uint16), "normed": normed.cpu().numpy().view(np.uint16),
+            "q": q.cpu().numpy(), "sf": sf.cpu().numpy()}
+
+
+def quant_outputs(torch, T, K, ldx):
+    from oracle import ref
+    x = quant_case(T, K, ldx)
+    dev = torch.device("cuda:0")
+    dx = torch.from_numpy(x.view(np.int16)).to(dev)
+    q = torch.zeros(T * K, dtype=torch.uint8, device=dev)
+    sf = torch.zeros((K + 511) // 512 * T * 4, dtype=torch.uint8, device=dev)
+    ref.quant(dx.data_ptr(), ldx, q.data_ptr(), sf.data_ptr(), T, K, T)
+    torch.cuda.synchronize()
+    return x, {"q": q.cpu().numpy(), "sf": sf.cpu().numpy()}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=str(HERE))
@@ -147,6 +178,11 @@ def main():
     for name, T, seed, full in Q_POST:
         c, res = q_post_outputs(torch, T, seed, full)
         digests[name] = {"input_sha": q_post_input_digest(c), **{k: sha(v) for k, v in res.items()}}
+    for name, T, K, ldx in QUANT:
+        x, res = quant_outputs(torch, T, K, ldx)
+        digests[name] = {"input_sha": sha(x), **{k: sha(v) for k, v in res.items()}}
+    for name, T, seed, with_a in NORM_SMALL:
+        np.savez_compressed(out / f"ref_small_{name}.npz", **norm_outputs(torch, T, seed, with_a))
     (out / "ref_digests.json").write_text(json.dumps(digests, indent=1, sort_keys=True) + "\n")
     print("golden vectors written to", out)
 

@@ -181,3 +181,27 @@ def q_post_case(T, seed, ldb=LDB):
             "iw": W.bf16_bits(rng.standard_normal((T, 32), dtype=np.float32)), "T": T, "ldb": ldb}
 
 
+
+
+def norm_case(T, seed, with_a=True):
+    """Inputs of glm_add_rms_quant: a, res [T, 6144] bf16 (rows scaled 0.05 .. 20; row 1 all zero), gamma."""
+    H = 6144
+    rng = np.random.default_rng(seed)
+    scale = rng.uniform(0.05, 20, (T, 1)).astype(np.float32)
+    res = W.bf16_bits(rng.standard_normal((T, H), dtype=np.float32) * scale)
+    a = W.bf16_bits(rng.standard_normal((T, H), dtype=np.float32) * scale) if with_a else None
+    gamma = W.bf16_bits(rng.uniform(0.5, 1.5, H).astype(np.float32))
+    if T > 2:
+        res[1] = 0  # an all-zero row (a too): rr = rsqrt(eps)
+        if a is not None:
+            a[1] = 0
+    return a, res, gamma
+
+
+def quant_case(T, K, ldx):
+    """Input of glm_quant: x [T, ldx] bf16, rows scaled 1e-3 .. 1e3, one all-zero block."""
+    rng = np.random.default_rng(T + K)
+    x = W.bf16_bits(rng.standard_normal((T, ldx), dtype=np.float32) * rng.uniform(1e-3, 1e3, (T, 1)))
+    if T > 2:
+        x[1, :128] = 0  # an all-zero block: scale from eps 1e-10
+    return x

@@ -231,3 +231,50 @@ def test_oracle_q_post_matches_reference_digests(name):
     assert _sha(qmla.reshape(T, 64, 576)[:, :, 512:]) == want["qmla_tails"]
     assert _sha(iq) == want["iq"]
     assert _sha(wout.view(np.uint32)) == want["wout"]
+
+
+@pytest.mark.parametrize("name", ["quant_640", "quant_16384"])
+def test_oracle_quant_matches_reference_digests(name):
+    path = GOLDEN / "ref_digests.json"
+    want = json.loads(path.read_text()) if path.exists() else {}
+    if name not in want:
+        pytest.skip("glm_quant golden vectors not generated yet (tests/golden/make_golden.py on a GPU)")
+    import sys
+    sys.path.insert(0, str(GOLDEN))
+    import make_golden as MG
+    from layer_case import quant_case
+
+    _, T, K, ldx = {q[0]: q for q in MG.QUANT}[name]
+    x = quant_case(T, K, ldx)
+    assert want[name]["input_sha"] == _sha(x), "input generator drifted from the recorded vectors"
+    q = np.zeros(T * K, np.uint8)
+    sf = np.zeros((K + 511) // 512 * T * 4, np.uint8)
+    cpu.quant(x, ldx, q, sf, T, K, T)
+    assert _sha(q) == want[name]["q"] and _sha(sf) == want[name]["sf"]
+
+
+@pytest.mark.parametrize("name", ["norm_add", "norm_noadd"])
+def test_oracle_add_rms_quant_matches_reference(name):
+    from compare import BF16_REL, E4M3_REL, assert_values_close, bf16_to_f32
+    path = GOLDEN / f"ref_small_{name}.npz"
+    if not path.exists():
+        pytest.skip("glm_add_rms_quant golden vectors not generated yet (tests/golden/make_golden.py on a GPU)")
+    ref = np.load(path)
+    import sys
+    sys.path.insert(0, str(GOLDEN))
+    import make_golden as MG
+    from layer_case import norm_case
+
+    _, T, seed, with_a = {n[0]: n for n in MG.NORM_SMALL}[name]
+    a, res, gamma = norm_case(T, seed, with_a)
+    normed = np.zeros(T * 6144, np.uint16)
+    q = np.zeros(T * 6144, np.uint8)
+    sf = np.zeros(12 * T * 4, np.uint8)
+    cpu.add_rms_quant(a, res, gamma, normed, q, sf, T, T)
+    assert_equal(res.reshape(-1), ref["res"].reshape(-1), f"{name}: res")
+    assert_values_close(bf16_to_f32(normed), bf16_to_f32(ref["normed"]), BF16_REL, f"{name}: normed")
+
+    def vals(qq, ss):
+        e = ss.reshape(12, T, 4).transpose(1, 0, 2).reshape(T, 48).astype(np.int32)
+        return cpu.f32_from_e4m3(qq).reshape(T, 48, 128) * np.ldexp(1.0, e - 127)[:, :, None]
+    assert_values_close(vals(q, sf), vals(ref["q"], ref["sf"]), E4M3_REL, f"{name}: q")
