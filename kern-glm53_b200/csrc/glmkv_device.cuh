@@ -193,33 +193,6 @@ __device__ __forceinline__ float max8_scatter(const float (&v)[8], int l) {
   return fmaxf(c, __shfl_xor_sync(FULL, c, 1));
 }
 
-// Max over the warp of sixteen per-lane values v[kb], scattered: lane l returns the max for
-// kb = l >> 1.
-__device__ __forceinline__ float max16_scatter(const float (&v)[16], int l) {
-  const bool b4 = l & 16, b3 = l & 8, b2 = l & 4, b1 = l & 2;
-  float a[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const float send = b4 ? v[k] : v[k + 8], keep = b4 ? v[k + 8] : v[k];
-    a[k] = fmaxf(keep, __shfl_xor_sync(FULL, send, 16));
-  }
-  float b[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float send = b3 ? a[k] : a[k + 4], keep = b3 ? a[k + 4] : a[k];
-    b[k] = fmaxf(keep, __shfl_xor_sync(FULL, send, 8));
-  }
-  float c[2];
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const float send = b2 ? b[k] : b[k + 2], keep = b2 ? b[k + 2] : b[k];
-    c[k] = fmaxf(keep, __shfl_xor_sync(FULL, send, 4));
-  }
-  const float send = b1 ? c[0] : c[1], keep = b1 ? c[1] : c[0];
-  const float d = fmaxf(keep, __shfl_xor_sync(FULL, send, 2));
-  return fmaxf(d, __shfl_xor_sync(FULL, d, 1));
-}
-
 // ------------------------------------------------------------------------------------------ mbarrier + TMA
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -107,6 +107,62 @@ __device__ __forceinline__ uint32_t absmax2_bf16x2(uint32_t a, uint32_t b) {
   return d;
 }
 
+// max(|a|, |b|) per bf16 half, with the sign bit the xor of the operands' (callers mask it off).
+__device__ __forceinline__ uint32_t absmax_xs(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// Max over the warp of eight per-lane bf16x2 words (xorsign-abs max), scattered: lane l returns
+// word (l >> 2) & 7.
+__device__ __forceinline__ uint32_t max8w_scatter(const uint32_t (&v)[8], int l) {
+  const bool b4 = l & 16, b3 = l & 8, b2 = l & 4;
+  uint32_t a[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t send = b4 ? v[k] : v[k + 4], keep = b4 ? v[k + 4] : v[k];
+    a[k] = absmax_xs(keep, __shfl_xor_sync(FULL, send, 16));
+  }
+  uint32_t b[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const uint32_t send = b3 ? a[k] : a[k + 2], keep = b3 ? a[k + 2] : a[k];
+    b[k] = absmax_xs(keep, __shfl_xor_sync(FULL, send, 8));
+  }
+  const uint32_t send = b2 ? b[0] : b[1], keep = b2 ? b[1] : b[0];
+  uint32_t c = absmax_xs(keep, __shfl_xor_sync(FULL, send, 4));
+  c = absmax_xs(c, __shfl_xor_sync(FULL, c, 2));
+  return absmax_xs(c, __shfl_xor_sync(FULL, c, 1));
+}
+
+// acc + w0^2 + w1^2 + w2^2 + w3^2 for the four bf16 values of v, in that order, each step one f32
+// FMA of the bf16 operands (fma.rn.f32.bf16: the product is exact, so it rounds like fmaf on the
+// widened values).
+__device__ __forceinline__ float sq_acc4(uint2 v, float acc) {
+  float d;
+  asm("{\n\t.reg .b16 a, b, c, d;\n\t"
+      "mov.b32 {a, b}, %1;\n\tmov.b32 {c, d}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, a, a, %3;\n\tfma.rn.f32.bf16 %0, b, b, %0;\n\t"
+      "fma.rn.f32.bf16 %0, c, c, %0;\n\tfma.rn.f32.bf16 %0, d, d, %0;\n\t}"
+      : "=f"(d)
+      : "r"(v.x), "r"(v.y), "f"(acc));
+  return d;
+}
+
+// The two bf16 values of w times s, as f32: one fma.rn.f32.bf16 each, whose addend -0 keeps the sign
+// of a zero product, so each rounds like the f32 multiply of the widened value. s is the f32 bit
+// pattern of a power of two (or 0 or inf) at least 2^-133: its low 16 bits are zero, so its high
+// half is the same number as a bf16.
+__device__ __forceinline__ float2 scale_bf16x2(uint32_t w, uint32_t s) {
+  float2 d;
+  asm("{\n\t.reg .b16 a, b, sl, sh;\n\t"
+      "mov.b32 {a, b}, %2;\n\tmov.b32 {sl, sh}, %3;\n\t"
+      "fma.rn.f32.bf16 %0, a, sh, 0f80000000;\n\tfma.rn.f32.bf16 %1, b, sh, 0f80000000;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "r"(w), "r"(s));
+  return d;
+}
+
 // A row's operands: the warp's shared-memory copy, or global memory when the row is not 16-byte
 // aligned for a bulk copy.
 struct SmemRow {
@@ -139,30 +195,11 @@ __device__ __forceinline__ void prep_row(const Row& row, const float* __restrict
   uint32_t csw = 0;  // rope[pos]: cs[2l], cs[2l + 1]
   if (s >= 0) csw = __ldg(reinterpret_cast<const unsigned*>(rope + (size_t)p * 2 * HALF) + l);
 
-  // ---- RMS factors (glm_glue.cu:212-221): per-thread sequential partials, block_sum order. Two
-  // virtual warps share an f32x2 accumulator; each half keeps its own sequence of FMAs.
+  // ---- RMS factors (glm_glue.cu:212-221): per-thread sequential partials, block_sum order. Virtual
+  // warp h sums its blocks 2h and 2h + 1 in column order, one FMA of the bf16 operands a value.
   float part[8];
-  {
-    float2 acc[4];
 #pragma unroll
-    for (int h = 0; h < 4; ++h) acc[h] = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        const uint2 a = qw[4 * h + i], b = qw[4 * h + 2 + i];  // blocks 2(2h) + i and 2(2h + 1) + i
-        float2 v = make_float2(bf_lo(a.x), bf_lo(b.x));
-        acc[h] = fma2(v, v, acc[h]);
-        v = make_float2(bf_hi(a.x), bf_hi(b.x));
-        acc[h] = fma2(v, v, acc[h]);
-        v = make_float2(bf_lo(a.y), bf_lo(b.y));
-        acc[h] = fma2(v, v, acc[h]);
-        v = make_float2(bf_hi(a.y), bf_hi(b.y));
-        acc[h] = fma2(v, v, acc[h]);
-      }
-#pragma unroll
-    for (int h = 0; h < 4; ++h) part[2 * h] = acc[h].x, part[2 * h + 1] = acc[h].y;
-  }
+  for (int h = 0; h < 8; ++h) part[h] = sq_acc4(qw[2 * h + 1], sq_acc4(qw[2 * h], 0.f));
   const float rq = rsqrtf(block_sum8(part, l) / 2048.f + EPS);
 #pragma unroll
   for (int h = 0; h < 4; ++h) {
@@ -176,29 +213,34 @@ __device__ __forceinline__ void prep_row(const Row& row, const float* __restrict
   // ---- q_c = bf16((q_a * rq) * g_q), e4m3 per 128 columns with UE8M0 scales (glm_glue.cu:222-230)
   const float2 rq2 = make_float2(rq, rq);
   uint32_t yb[16][2];
-  float am[16];
 #pragma unroll
   for (int kb = 0; kb < 16; ++kb) {
     const float4 g = *reinterpret_cast<const float4*>(wq + kb * 128 + 4 * l);
     yb[kb][0] = round2(mul2(mul2(unpack2(qw[kb].x), rq2), make_float2(g.x, g.y)));
     yb[kb][1] = round2(mul2(mul2(unpack2(qw[kb].y), rq2), make_float2(g.z, g.w)));
-    const uint32_t m = absmax2_bf16x2(yb[kb][0], yb[kb][1]);
-    am[kb] = fmaxf(bf_lo(m), bf_hi(m));
   }
+  // |max| of this lane's values of blocks 2j (low half) and 2j + 1 (high half), then over the warp
+  uint32_t m2[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t a = absmax_xs(yb[2 * j][0], yb[2 * j][1]), b = absmax_xs(yb[2 * j + 1][0], yb[2 * j + 1][1]);
+    m2[j] = absmax_xs(__byte_perm(a, b, 0x5410), __byte_perm(a, b, 0x7632));
+  }
+  const uint32_t mw = max8w_scatter(m2, l);  // lane l: blocks 2 ((l >> 2) & 7) and 2 ((l >> 2) & 7) + 1
+  const float bm = __uint_as_float(((l & 1) ? (mw & 0xffff0000u) : (mw << 16)) & 0x7fffffffu);
   unsigned e;
-  const float inv = __frcp_rn(ue8m0_div(max16_scatter(am, l), 1e-10f, &e));  // lane l: block kb = l >> 1
+  const float inv = __frcp_rn(ue8m0_div(bm, 1e-10f, &e));  // lane l: block 2 ((l >> 2) & 7) + (l & 1)
   u8* qrow = qq + (size_t)r * QL;
 #pragma unroll
   for (int kb = 0; kb < 16; ++kb) {
-    const float iv = __shfl_sync(FULL, inv, 2 * kb);
-    const float2 iv2 = make_float2(iv, iv);
-    const float2 a = mul2(unpack2(yb[kb][0]), iv2), b = mul2(unpack2(yb[kb][1]), iv2);
+    const uint32_t iv = __shfl_sync(FULL, __float_as_uint(inv), 4 * (kb >> 1) + (kb & 1));
+    const float2 a = scale_bf16x2(yb[kb][0], iv), b = scale_bf16x2(yb[kb][1], iv);
     *reinterpret_cast<uint32_t*>(qrow + kb * 128 + 4 * l) = fp8x4(a.x, a.y, b.x, b.y);
   }
   // DeepGEMM's packed scales: byte (kb & 3) of word (kb >> 2, r); lane q < 4 writes word q whole.
   unsigned word = 0;
 #pragma unroll
-  for (int m = 0; m < 4; ++m) word |= __shfl_sync(FULL, e, 2 * (4 * (l & 3) + m)) << (8 * m);
+  for (int m = 0; m < 4; ++m) word |= __shfl_sync(FULL, e, 8 * (l & 3) + 4 * (m >> 1) + (m & 1)) << (8 * m);
   if (l < 4) *reinterpret_cast<unsigned*>(qsf + ((size_t)l * sf_rows + r) * 4) = word;
 
   if (s < 0) return;  // no cache slot: nothing more to write (glm_glue.cu:231-232)
@@ -212,20 +254,27 @@ __device__ __forceinline__ void prep_row(const Row& row, const float* __restrict
   u8* dst = kv + s * (FP8 ? KV8 : KVB);
   if constexpr (FP8) {
     // tiles of 128 (two virtual warps), scale amax / 448, e4m3 satfinite (glm_glue.cu:238-247)
-    float m8[8];
+    // |max| per bf16 half of tile t (virtual warps 2t, 2t + 1); tiles 0 | 1 and 2 | 3 share a word,
+    // which a reduce-scatter over the warp leaves in lanes < 16 and >= 16.
+    const uint32_t t0 = absmax_xs(kn[0], kn[1]), t1 = absmax_xs(kn[2], kn[3]);
+    const uint32_t t2 = absmax_xs(kn[4], kn[5]), t3 = absmax_xs(kn[6], kn[7]);
+    const uint32_t p01 = absmax_xs(__byte_perm(t0, t1, 0x5410), __byte_perm(t0, t1, 0x7632));
+    const uint32_t p23 = absmax_xs(__byte_perm(t2, t3, 0x5410), __byte_perm(t2, t3, 0x7632));
+    const bool b4 = l & 16;
+    uint32_t m = absmax_xs(b4 ? p23 : p01, __shfl_xor_sync(FULL, b4 ? p01 : p23, 16));
 #pragma unroll
-    for (int w = 0; w < 8; ++w) m8[w] = absmax_bf16x2(kn[w]);
-    const float wm = max8_scatter(m8, l);                     // lane l: warp (l >> 2) & 7
-    const float tm = fmaxf(wm, __shfl_xor_sync(FULL, wm, 4));  // lane l: tile (l >> 3) & 3
+    for (int o = 8; o > 0; o >>= 1) m = absmax_xs(m, __shfl_xor_sync(FULL, m, o));
+    // lane l: tile 2 (l >> 4) + (l & 1)
+    const float tm = __uint_as_float(((l & 1) ? (m & 0xffff0000u) : (m << 16)) & 0x7fffffffu);
     const float sc = __fdiv_rn(tm, 448.f);
     const float tinv = sc > 0.f ? __frcp_rn(sc) : 0.f;
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
-      const float iv = __shfl_sync(FULL, tinv, 8 * (w >> 1));
+      const float iv = __shfl_sync(FULL, tinv, 16 * (w >> 2) + ((w >> 1) & 1));
       const float2 q = mul2(unpack2(kn[w]), make_float2(iv, iv));
       *reinterpret_cast<uint16_t*>(dst + 2 * (32 * w + l)) = fp8x2(q.x, q.y);
     }
-    const float sct = __shfl_sync(FULL, sc, 8 * (l & 3));
+    const float sct = __shfl_sync(FULL, sc, 16 * ((l & 3) >> 1) + (l & 1));
     if (l < 4) reinterpret_cast<float*>(dst + KVL)[l] = sct;
   } else {
 #pragma unroll
@@ -307,22 +356,10 @@ __device__ __forceinline__ void prep_rows(const bf16* __restrict__ x, int lda, c
   }
   pdl_trigger();  // a persistent grid: all of its CTAs are resident
   pdl_wait();
-  for (int i = tid; i < QL; i += PREP_THREADS) wq[i] = __bfloat162float(g_q[i]);
-  for (int i = tid; i < KVL; i += PREP_THREADS) wkv[i] = __bfloat162float(g_kv[i]);
-  if (idx != nullptr)
-    for (int i = tid; i < ID; i += PREP_THREADS) wik[i] = __bfloat162float(ik_w[i]), wib[i] = __bfloat162float(ik_b[i]);
-  __syncthreads();
 
   const int stride = gridDim.x * PREP_WARPS;
   int r = blockIdx.x * PREP_WARPS + warp;
-  if (r >= T) return;
   const bool bulk = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (lda & 7) == 0;
-  if (!bulk) {
-    for (; r < T; r += stride)
-      prep_row<FP8>(GlobalRow{reinterpret_cast<const u8*>(x + (size_t)r * lda)}, wq, wkv, wik, wib, rope, pos[r],
-                    slot[r], kv, idx, qq, qsf, sf_rows, r, l);
-    return;
-  }
   const uint32_t bytes = idx != nullptr ? PREP_ROW : 2 * (QL + MLA);
   u8* buf = smem + PREP_WGT + (size_t)warp * PREP_BUFS * PREP_ROW;
   auto issue = [&](int b, int row) {
@@ -331,7 +368,35 @@ __device__ __forceinline__ void prep_rows(const bf16* __restrict__ x, int lda, c
     mbar_arrive_expect_tx(mb, bytes);
     tma_load_1d(smem_u32(buf + b * PREP_ROW), x + (size_t)row * lda, bytes, mb);
   };
-  if (l == 0) issue(0, r);
+  if (bulk && r < T && l == 0) issue(0, r);  // the warp's first row is on its way while the weights are staged
+
+  // The norm weights as f32, every load in flight at once (g_q and the indexer weights 8-byte aligned,
+  // g_kv 4-byte aligned; the launcher checks).
+  {
+    const uint2 q0 = __ldg(reinterpret_cast<const uint2*>(g_q) + tid);
+    const uint2 q1 = __ldg(reinterpret_cast<const uint2*>(g_q) + PREP_THREADS + tid);
+    const uint32_t k0 = __ldg(reinterpret_cast<const unsigned*>(g_kv) + tid);
+    const bool wi = idx != nullptr && tid < ID / 2;
+    uint2 w = make_uint2(0u, 0u);
+    if (wi) w = __ldg(reinterpret_cast<const uint2*>(tid < ID / 4 ? ik_w : ik_b) + (tid & (ID / 4 - 1)));
+    static_assert(QL == 8 * PREP_THREADS && KVL == 2 * PREP_THREADS, "one pass of loads stages g_q and g_kv");
+    *reinterpret_cast<float4*>(wq + 4 * tid) = make_float4(bf_lo(q0.x), bf_hi(q0.x), bf_lo(q0.y), bf_hi(q0.y));
+    *reinterpret_cast<float4*>(wq + 4 * (PREP_THREADS + tid)) =
+        make_float4(bf_lo(q1.x), bf_hi(q1.x), bf_lo(q1.y), bf_hi(q1.y));
+    *reinterpret_cast<float2*>(wkv + 2 * tid) = make_float2(bf_lo(k0), bf_hi(k0));
+    if (wi)
+      *reinterpret_cast<float4*>((tid < ID / 4 ? wik : wib) + 4 * (tid & (ID / 4 - 1))) =
+          make_float4(bf_lo(w.x), bf_hi(w.x), bf_lo(w.y), bf_hi(w.y));
+  }
+  __syncthreads();
+
+  if (r >= T) return;
+  if (!bulk) {
+    for (; r < T; r += stride)
+      prep_row<FP8>(GlobalRow{reinterpret_cast<const u8*>(x + (size_t)r * lda)}, wq, wkv, wik, wib, rope, pos[r],
+                    slot[r], kv, idx, qq, qsf, sf_rows, r, l);
+    return;
+  }
   int p = pos[r];
   long long s = slot[r];
   for (int k = 0; r < T; ++k, r += stride) {
