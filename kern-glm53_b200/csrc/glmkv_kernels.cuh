@@ -113,6 +113,17 @@ __device__ __forceinline__ uint32_t absmax_xs(uint32_t a, uint32_t b) {
   asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
+// bf16x2 add and multiply, each half rounded once from the exact result (sm_90+).
+__device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 // Max over the warp of eight per-lane bf16x2 words (xorsign-abs max), scattered: lane l returns
 // word (l >> 2) & 7.
 __device__ __forceinline__ uint32_t max8w_scatter(const uint32_t (&v)[8], int l) {
@@ -807,18 +818,6 @@ __device__ __forceinline__ float absmax8_bf16(uint4 v) {
   return absmax_bf16x2(absmax2_bf16x2(absmax2_bf16x2(v.x, v.y), absmax2_bf16x2(v.z, v.w)));
 }
 
-// One 128-column block held four values a lane by a whole warp, quantized (glm_glue.cu:86-92):
-// amax over the warp, UE8M0 scale (eps 1e-10), e4m3 of y * (1 / scale); lane 0 writes the byte.
-__device__ __forceinline__ void quant_warp4(const float (&y)[4], u8* __restrict__ q, u8* __restrict__ sf, int sf_rows,
-                                            int r, int kb, int l) {
-  const float amax = warp_max(fmaxf(fmaxf(fabsf(y[0]), fabsf(y[1])), fmaxf(fabsf(y[2]), fabsf(y[3]))));
-  const unsigned e = ue8m0_byte(amax, 1e-10f);
-  const float inv = ue8m0_inv(e);
-  *reinterpret_cast<uint32_t*>(q) = fp8x4(__fmul_rn(y[0], inv), __fmul_rn(y[1], inv), __fmul_rn(y[2], inv),
-                                          __fmul_rn(y[3], inv));
-  if (l == 0) sf[((size_t)(kb >> 2) * sf_rows + r) * 4 + (kb & 3)] = (u8)e;
-}
-
 }  // namespace glmkv
 
 // res = bf16(a + res) (a null: res is already the stream), written back; normed = bf16(bf16(res * rr)
@@ -874,22 +873,23 @@ extern "C" __global__ void __launch_bounds__(glmkv::ARQ_THREADS, 3)
     }
     const u8* srow = smem + (size_t)st * 2 * ARQ_ROW;
     bf16* row = res + (size_t)r * HID;
-    float v[6][4], ss = 0.f;
+    // v = bf16(a + res): add.rn.bf16x2 rounds the exact sum once, which equals the reference's f32
+    // add then bf16 round for every pair of bf16 operands (double rounding through f32 is harmless
+    // for bf16; tests/bf16_identities.cu checks all 2^32 pairs). The squares are summed in the
+    // thread's column order, one mixed-precision FMA a value.
+    uint2 vw[6];
+    float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < 6; ++i) {
       const int c = (w * 6 + i) * 128 + l * 4;
-      const uint2 rv = *reinterpret_cast<const uint2*>(srow + 2 * c);
-      v[i][0] = bf_lo(rv.x), v[i][1] = bf_hi(rv.x), v[i][2] = bf_lo(rv.y), v[i][3] = bf_hi(rv.y);
+      uint2 rv = *reinterpret_cast<const uint2*>(srow + 2 * c);
       if (has_a) {
         const uint2 av = *reinterpret_cast<const uint2*>(srow + ARQ_ROW + 2 * c);
-        v[i][0] = rnd(__fadd_rn(v[i][0], bf_lo(av.x)));
-        v[i][1] = rnd(__fadd_rn(v[i][1], bf_hi(av.x)));
-        v[i][2] = rnd(__fadd_rn(v[i][2], bf_lo(av.y)));
-        v[i][3] = rnd(__fadd_rn(v[i][3], bf_hi(av.y)));
-        *reinterpret_cast<uint2*>(row + c) = make_uint2(pack_bf16x2(v[i][0], v[i][1]), pack_bf16x2(v[i][2], v[i][3]));
+        rv = make_uint2(add_bf16x2(rv.x, av.x), add_bf16x2(rv.y, av.y));
+        *reinterpret_cast<uint2*>(row + c) = rv;
       }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) ss = __fmaf_rn(v[i][j], v[i][j], ss);  // squares of bf16 values: exact
+      vw[i] = rv;
+      ss = sq_acc4(rv, ss);
     }
     // the reference's block_sum (glm_glue.cu:57-65): warp butterflies, then the eight warp totals
     ss = warp_sum(ss);
@@ -898,17 +898,45 @@ extern "C" __global__ void __launch_bounds__(glmkv::ARQ_THREADS, 3)
     __syncthreads();
     const float tot = warp_sum(l < 8 ? sm[l] : 0.f);
     const float rr = rsqrtf(__fadd_rn(__fdiv_rn(tot, (float)HID), EPS));
+    // y = bf16(bf16(v * rr) * gamma): the first product in f32, rounded; the second is exact in f32,
+    // so mul.rn.bf16x2 rounds it identically.
+    const float2 rr2 = make_float2(rr, rr);
+    uint2 yw[6];
 #pragma unroll
     for (int i = 0; i < 6; ++i) {
-      const int kb = w * 6 + i, c = kb * 128 + l * 4;
-      const float g[4] = {bf_lo(gw[i].x), bf_hi(gw[i].x), bf_lo(gw[i].y), bf_hi(gw[i].y)};
-      float y[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) y[j] = rnd(__fmul_rn(rnd(__fmul_rn(v[i][j], rr)), g[j]));
-      if (normed != nullptr)
-        *reinterpret_cast<uint2*>(normed + (size_t)r * HID + c) = make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
-      if (q != nullptr) quant_warp4(y, q + (size_t)r * HID + c, sf, sf_rows, r, kb, l);
+      yw[i].x = mul_bf16x2(round2(mul2(unpack2(vw[i].x), rr2)), gw[i].x);
+      yw[i].y = mul_bf16x2(round2(mul2(unpack2(vw[i].y), rr2)), gw[i].y);
+      if (normed != nullptr) *reinterpret_cast<uint2*>(normed + (size_t)r * HID + (w * 6 + i) * 128 + l * 4) = yw[i];
     }
+    if (q == nullptr) continue;
+    // Per 128-column block (glm_glue.cu:86-92): the warp's six blocks' |max| in three packed words
+    // (blocks 2j | 2j + 1), reduced and scattered so lane l holds block 2 ((l >> 3) & 3) + (l & 1)
+    // (lanes 24..31 hold padding); UE8M0 scale (eps 1e-10) there, then e4m3 of y * (1 / scale).
+    uint32_t m2[4];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const uint32_t x0 = absmax_xs(yw[2 * j].x, yw[2 * j].y), x1 = absmax_xs(yw[2 * j + 1].x, yw[2 * j + 1].y);
+      m2[j] = absmax_xs(__byte_perm(x0, x1, 0x5410), __byte_perm(x0, x1, 0x7632));
+    }
+    m2[3] = 0u;
+    const bool b4 = l & 16, b3 = l & 8;
+    const uint32_t a0 = absmax_xs(b4 ? m2[2] : m2[0], __shfl_xor_sync(FULL, b4 ? m2[0] : m2[2], 16));
+    const uint32_t a1 = absmax_xs(b4 ? m2[3] : m2[1], __shfl_xor_sync(FULL, b4 ? m2[1] : m2[3], 16));
+    uint32_t mw = absmax_xs(b3 ? a1 : a0, __shfl_xor_sync(FULL, b3 ? a0 : a1, 8));
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) mw = absmax_xs(mw, __shfl_xor_sync(FULL, mw, o));
+    const float bm = __uint_as_float(((l & 1) ? (mw & 0xffff0000u) : (mw << 16)) & 0x7fffffffu);
+    const unsigned e = ue8m0_byte(bm, 1e-10f);
+    const uint32_t inv = __float_as_uint(ue8m0_inv(e));
+    u8* qrow = q + (size_t)r * HID;
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+      const uint32_t iv = __shfl_sync(FULL, inv, 8 * (i >> 1) + (i & 1));
+      const float2 p0 = scale_bf16x2(yw[i].x, iv), p1 = scale_bf16x2(yw[i].y, iv);
+      *reinterpret_cast<uint32_t*>(qrow + (w * 6 + i) * 128 + l * 4) = fp8x4(p0.x, p0.y, p1.x, p1.y);
+    }
+    const int bk = 2 * ((l >> 3) & 3) + (l & 1), kb = w * 6 + bk;
+    if ((l & 6) == 0 && bk < 6) sf[((size_t)(kb >> 2) * sf_rows + r) * 4 + (kb & 3)] = (u8)e;
   }
 }
 
