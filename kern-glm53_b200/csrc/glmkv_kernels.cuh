@@ -687,6 +687,32 @@ constexpr int HEADS = 64, QHD = 256, NOPE = 192, IH = 32;
 constexpr int QP_WARPS = 8;  // a CTA: 8 warps, one row each
 constexpr int QP_THREADS = 32 * QP_WARPS;
 
+// (x1 c - x2 s, x2 c + x1 s) of the bf16 pair w = (x1, x2), as bf16 RN, with c, s and -s the bf16
+// in half H of cw, sw and nsw. Both products of each output are bf16 x bf16, exact in f32, so the
+// mixed-precision FMAs round exactly as the reference's fmaf(x1, c, -(x2 * s)) and
+// fmaf(x2, c, x1 * s) on widened values; the addend -0 keeps the sign of a zero product.
+template <int H>
+__device__ __forceinline__ uint32_t rope_bf16(uint32_t w, uint32_t cw, uint32_t sw, uint32_t nsw) {
+  uint32_t d;
+  if constexpr (H == 0)
+    asm("{\n\t.reg .b16 x1, x2, c, s, ns, z;\n\t.reg .f32 t, u, o1, o2;\n\t"
+        "mov.b32 {x1, x2}, %1;\n\tmov.b32 {c, z}, %2;\n\tmov.b32 {s, z}, %3;\n\tmov.b32 {ns, z}, %4;\n\t"
+        "fma.rn.f32.bf16 t, x2, ns, 0f80000000;\n\tfma.rn.f32.bf16 o1, x1, c, t;\n\t"
+        "fma.rn.f32.bf16 u, x1, s, 0f80000000;\n\tfma.rn.f32.bf16 o2, x2, c, u;\n\t"
+        "cvt.rn.bf16x2.f32 %0, o2, o1;\n\t}"
+        : "=r"(d)
+        : "r"(w), "r"(cw), "r"(sw), "r"(nsw));
+  else
+    asm("{\n\t.reg .b16 x1, x2, c, s, ns, z;\n\t.reg .f32 t, u, o1, o2;\n\t"
+        "mov.b32 {x1, x2}, %1;\n\tmov.b32 {z, c}, %2;\n\tmov.b32 {z, s}, %3;\n\tmov.b32 {z, ns}, %4;\n\t"
+        "fma.rn.f32.bf16 t, x2, ns, 0f80000000;\n\tfma.rn.f32.bf16 o1, x1, c, t;\n\t"
+        "fma.rn.f32.bf16 u, x1, s, 0f80000000;\n\tfma.rn.f32.bf16 o2, x2, c, u;\n\t"
+        "cvt.rn.bf16x2.f32 %0, o2, o1;\n\t}"
+        : "=r"(d)
+        : "r"(w), "r"(cw), "r"(sw), "r"(nsw));
+  return d;
+}
+
 // A row of q_b's output after the W_UK absorb (glm_glue.cu:301-351), by ONE warp:
 //  - q_pe rope into the tail of each head of qmla [T, 64, 576]: lane l owns pairs 4q .. 4q + 3
 //    (q = l & 7) of heads 4k + (l >> 3), k = 0..15, so every load and store is 16 bytes and a warp
@@ -698,7 +724,7 @@ constexpr int QP_THREADS = 32 * QP_WARPS;
 // Every rope product is bf16 x bf16, exact in f32, so the rounding is the reference's whatever the
 // contraction. sc is a power of two, so v * (1 / sc) rounds exactly as v / sc. All of the row's
 // q_pe loads and the first eight heads of the query are in flight before any arithmetic.
-template <bool FULL>
+template <bool INDEXER>
 __device__ __forceinline__ void q_post_row(const bf16* __restrict__ qb, int ldb, const bf16* __restrict__ rope, int p,
                                            bf16* __restrict__ qmla, u8* __restrict__ iq, const bf16* __restrict__ iw,
                                            float* __restrict__ wout, int r, int l) {
@@ -709,28 +735,25 @@ __device__ __forceinline__ void q_post_row(const bf16* __restrict__ qb, int ldb,
 #pragma unroll
   for (int k = 0; k < 16; ++k) v[k] = ld_stream_v4u(row + 2 * ((4 * k + (l >> 3)) * QHD + NOPE) + 16 * q);
   uint2 g0[8];  // the indexer query's heads 0..7, dims 4l .. 4l + 3
-  if constexpr (FULL) {
+  if constexpr (INDEXER) {
 #pragma unroll
     for (int k = 0; k < 8; ++k) g0[k] = ld_stream_v2(row + 2 * (HEADS * QHD + k * ID + 4 * l));
   }
   // rope values of this lane's pairs 4q .. 4q + 3: cos at cs[4q ..], sin at cs[32 + 4q ..]
   const uint2 cw = __ldg(reinterpret_cast<const uint2*>(cs) + q), sw = __ldg(reinterpret_cast<const uint2*>(cs + 16) + q);
-  const float c[4] = {bf_lo(cw.x), bf_hi(cw.x), bf_lo(cw.y), bf_hi(cw.y)};
-  const float sn[4] = {bf_lo(sw.x), bf_hi(sw.x), bf_lo(sw.y), bf_hi(sw.y)};
+  const uint2 nsw = make_uint2(sw.x ^ 0x80008000u, sw.y ^ 0x80008000u);
   u8* out = reinterpret_cast<u8*>(qmla + (size_t)r * HEADS * MLA);
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
     const int h = 4 * k + (l >> 3);
-    const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-    uint32_t o[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float x1 = bf_lo(w[i]), x2 = bf_hi(w[i]);
-      o[i] = pack_bf16x2(__fmaf_rn(x1, c[i], -__fmul_rn(x2, sn[i])), __fmaf_rn(x2, c[i], __fmul_rn(x1, sn[i])));
-    }
-    *reinterpret_cast<uint4*>(out + 2 * (h * MLA + KVL) + 16 * q) = make_uint4(o[0], o[1], o[2], o[3]);
+    uint4 o;
+    o.x = rope_bf16<0>(v[k].x, cw.x, sw.x, nsw.x);
+    o.y = rope_bf16<1>(v[k].y, cw.x, sw.x, nsw.x);
+    o.z = rope_bf16<0>(v[k].z, cw.y, sw.y, nsw.y);
+    o.w = rope_bf16<1>(v[k].w, cw.y, sw.y, nsw.y);
+    *reinterpret_cast<uint4*>(out + 2 * (h * MLA + KVL) + 16 * q) = o;
   }
-  if constexpr (FULL) {
+  if constexpr (INDEXER) {
     // lane l < 16 ropes dims 4l .. 4l + 3 (pairs 2l, 2l + 1)
     const unsigned c2 = l < 16 ? __ldg(cs + l) : 0u, s2 = l < 16 ? __ldg(cs + 16 + l) : 0u;
     const float ca = bf_lo(c2), sa = bf_lo(s2), cb = bf_hi(c2), sb = bf_hi(s2);

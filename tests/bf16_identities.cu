@@ -5,6 +5,7 @@
 //   mul.rn.bf16x2 (a, b)              == bf16_rn(f32 a * f32 b)            all 2^32 bf16 pairs
 //   fma.rn.f32.bf16 (y, s, -0)        == f32 y * f32 s                     all 2^32 bf16 pairs
 //   fma.rn.f32.bf16 (a, a, c)         == fmaf(f32 a, f32 a, c)             all bf16 a x 2^16 f32 c
+//   fma.rn.f32.bf16 (a, b, c)         == fmaf(f32 a, f32 b, c)             all 2^32 bf16 pairs, c hashed
 //   max.xorsign.abs.bf16x2 (a, b)     == fmaxf(|f32 a|, |f32 b|)           all 2^32 bf16 pairs
 //                                        (magnitude; NaN-vs-NaN encodings counted apart)
 //
@@ -22,7 +23,7 @@ __device__ __forceinline__ uint32_t bf16_rn(float x) {
 }
 __device__ __forceinline__ bool nan16(uint32_t h) { return (h & 0x7f80u) == 0x7f80u && (h & 0x7fu) != 0u; }
 
-enum { ADD, MUL, SCALE, SQ, MAXABS, NCHECK };
+enum { ADD, MUL, SCALE, SQ, FMA, MAXABS, NCHECK };
 
 __global__ void check_pairs(unsigned long long* bad, unsigned long long* nan_only) {
   unsigned long long b[NCHECK] = {}, n[NCHECK] = {};
@@ -57,6 +58,19 @@ __global__ void check_pairs(unsigned long long* bad, unsigned long long* nan_onl
     asm("{\n\t.reg .b16 p, z;\n\tmov.b32 {p, z}, %1;\n\tfma.rn.f32.bf16 %0, p, p, %2;\n\t}" : "=f"(e) : "r"(a), "f"(acc));
     const float want_e = __fmaf_rn(widen(a), widen(a), acc);
     if (__float_as_uint(e) != __float_as_uint(want_e)) ++(e != e && want_e != want_e ? n[SQ] : b[SQ]);
+    // a * c + an addend near the product's magnitude (exponent of a * c, +-24) or anywhere, by a hash of i
+    const uint32_t hsh = (uint32_t)(i * 0x9E3779B97F4A7C15ull >> 32);
+    const float pr = __fmul_rn(widen(a), widen(c));
+    const uint32_t pe = (__float_as_uint(pr) >> 23) & 0xffu;
+    const uint32_t ae = (hsh & 1u) ? (hsh >> 24) : (uint32_t)min(254, max(1, (int)pe + (int)((hsh >> 24) % 49u) - 24));
+    const float addend = __uint_as_float((hsh & 0x80000000u) | (ae << 23) | ((hsh >> 1) & 0x7fffffu));
+    float f;
+    asm("{\n\t.reg .b16 p, q, z;\n\tmov.b32 {p, z}, %1;\n\tmov.b32 {q, z}, %2;\n\t"
+        "fma.rn.f32.bf16 %0, p, q, %3;\n\t}"
+        : "=f"(f)
+        : "r"(a), "r"(c), "f"(addend));
+    const float want_f = __fmaf_rn(widen(a), widen(c), addend);
+    if (__float_as_uint(f) != __float_as_uint(want_f)) ++(f != f && want_f != want_f ? n[FMA] : b[FMA]);
   }
   for (int k = 0; k < NCHECK; ++k) {
     if (b[k]) atomicAdd(bad + k, b[k]);
@@ -77,7 +91,7 @@ int main() {
     return 2;
   }
   const char* names[NCHECK] = {"add.rn.bf16x2", "mul.rn.bf16x2", "fma.rn.f32.bf16(y,s,-0)", "fma.rn.f32.bf16(a,a,c)",
-                               "max.xorsign.abs.bf16x2"};
+                               "fma.rn.f32.bf16(a,b,c)", "max.xorsign.abs.bf16x2"};
   unsigned long long total = 0;
   for (int k = 0; k < NCHECK; ++k) {
     printf("%s=%llu/%llu ", names[k], hb[k], hn[k]);

@@ -83,6 +83,35 @@ def test_layer_vs_reference_and_oracle(cuda, name, kv_dtype, full, zero_tiles):
         assert_equal(got["kvd"], kvd, f"{name} vs oracle: kvd")
 
 
+@pytest.mark.parametrize("kv_dtype,full", [("fp8", True), ("fp8", False), ("bf16", True)])
+def test_append_padding_rows_skip_the_caches(cuda, kv_dtype, full):
+    """Rows with slot < 0 (padding) still get their q quant but write no cache row (glm_glue.cu:231-232):
+    bit-exact against the reference, and the caches equal the oracle's everywhere else."""
+    from glmkv import workload as W
+    from oracle import cpu
+
+    call = W.config("cfg0", seed=3)
+    call.slot_mapping[::7] = -1
+    call.slot_mapping[-3:] = -1  # the last rows of the call, and so of the last warp's share
+    case = LayerCase(call, kv_dtype=kv_dtype, seed=13)
+    got, ref = _run_both(case, cuda, full)
+    if ref is not None:
+        _assert_all_equal(got, ref, f"padding rows/{kv_dtype}/{'full' if full else 'shared'} vs reference")
+    h = case.host()
+    run_oracle(case, h, full)
+    assert_prep_close(got, h, case, full, what="padding rows vs oracle")
+    # every cache row but the live slots is the input pool, untouched
+    row = 656 if kv_dtype == "fp8" else 1152
+    live = call.slot_mapping[call.slot_mapping >= 0]
+    untouched = np.setdiff1d(np.arange(call.n_pages * 64), live)
+    assert_equal(got["kv"].reshape(-1, row)[untouched], case.kv_pool.reshape(-1, row)[untouched], "kv rows not written")
+    if full:
+        pages = got["idx"].reshape(-1, 64 * 132)
+        keys = pages[:, :8192].reshape(-1, 128)
+        assert_equal(keys[untouched], case.idx_pool.reshape(-1, 64 * 132)[:, :8192].reshape(-1, 128)[untouched],
+                     "indexer keys not written")
+
+
 @needs_ref
 def test_dequant_all_codes_vs_reference(cuda):
     """Every e4m3 code (NaN included) and scales over 24 binades: identical bits to the reference."""
