@@ -11,7 +11,7 @@ torch = pytest.importorskip("torch")
 
 CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES = 8
 ENTRIES = ("glm_plan", "glm_mla_prep", "glm_mla_prep_fp8", "glm_idx_gather", "glm_kv_dequant", "glm_topk_stream",
-           "glm_topk_slots")
+           "glm_topk_slots", "glm_q_post", "glm_add_rms_quant", "glm_quant")
 
 
 class Driver:
@@ -31,7 +31,7 @@ class Driver:
 
     def launch(self, name, grid, block, smem, args):
         f = self.function(name)
-        if smem > 48 * 1024:
+        if smem > 0:  # dynamic plus static shared memory above 48 KB needs the opt-in
             self._ok(self.cu.cuFuncSetAttribute(f, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, ctypes.c_int(smem)),
                      "cuFuncSetAttribute")
         vals = [ctypes.c_uint64(a) if isinstance(a, PtrArg) else ctypes.c_int(a) for a in args]
@@ -86,5 +86,74 @@ def test_cubin_entries_match_the_library(cuda):
         a, bb = to_host(lib_d, torch), to_host(cub_d, torch)
         for k in a:
             assert np.array_equal(a[k], bb[k]), k
+    finally:
+        drv.close()
+
+
+def test_cubin_glue_entries_match_the_library(cuda):
+    """glm_q_post, glm_add_rms_quant and glm_quant from the cubin, launched through the driver API,
+    against the library's launchers on the same inputs."""
+    import glmkv
+    from layer_case import LDB, norm_case, q_post_case, quant_case
+
+    drv = Driver(glmkv.CUBIN_PATH)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    try:
+        T = 300
+        c = q_post_case(T, 71)
+        qb, rope, pos, iw = t(c["qb"].view(np.int16)), t(c["rope"].view(np.int16)), t(c["pos"]), t(c["iw"].view(np.int16))
+        for full in (1, 0):
+            outs = []
+            for via in ("lib", "cubin"):
+                qmla = torch.zeros(T * 64 * 576, dtype=torch.int16, device=cuda)
+                iq = torch.zeros(T * 32 * 128, dtype=torch.uint8, device=cuda)
+                wout = torch.zeros(T * 32, dtype=torch.float32, device=cuda)
+                args = [P(qb), LDB, P(rope), P(pos), P(qmla), P(iq if full else None), P(iw if full else None),
+                        P(wout if full else None), full, T]
+                if via == "lib":
+                    glmkv.q_post_full(*[a if not isinstance(a, PtrArg) else int(a) for a in args])
+                else:
+                    g, b, sm = glmkv.launch_shape("glm_q_post", T)
+                    drv.launch("glm_q_post", g, b, sm, args)
+                torch.cuda.synchronize()
+                outs.append([x.cpu().numpy().view(np.uint8) for x in (qmla, iq, wout)])
+            for x, y in zip(*outs):
+                assert np.array_equal(x, y), f"q_post full={full}"
+
+        a_, res_, gamma = norm_case(64, 72, True)
+        for with_a in (True, False):
+            outs = []
+            for via in ("lib", "cubin"):
+                res = t(res_.view(np.int16))
+                normed = torch.zeros(64 * 6144, dtype=torch.int16, device=cuda)
+                q = torch.zeros(64 * 6144, dtype=torch.uint8, device=cuda)
+                sf = torch.zeros(12 * 64 * 4, dtype=torch.uint8, device=cuda)
+                args = [P(t(a_.view(np.int16)) if with_a else None), P(res), P(t(gamma.view(np.int16))), P(normed), P(q),
+                        P(sf), 64, 64]
+                if via == "lib":
+                    glmkv.add_rms_quant(*[int(a) if isinstance(a, PtrArg) else a for a in args])
+                else:
+                    g, b, sm = glmkv.launch_shape("glm_add_rms_quant", 64)
+                    drv.launch("glm_add_rms_quant", g, b, sm, args)
+                torch.cuda.synchronize()
+                outs.append([x.cpu().numpy().view(np.uint8) for x in (res, normed, q, sf)])
+            for x, y in zip(*outs):
+                assert np.array_equal(x, y), f"add_rms_quant with_a={with_a}"
+
+        T, K, ldx = 37, 640, 648
+        x = t(quant_case(T, K, ldx).view(np.int16))
+        outs = []
+        for via in ("lib", "cubin"):
+            q = torch.zeros(T * K, dtype=torch.uint8, device=cuda)
+            sf = torch.zeros((K + 511) // 512 * T * 4, dtype=torch.uint8, device=cuda)
+            args = [P(x), ldx, P(q), P(sf), T, K, T]
+            if via == "lib":
+                glmkv.quant_o(*[int(a) if isinstance(a, PtrArg) else a for a in args])
+            else:  # grid ceil(T * ceil(K / 512) / 8), block 256 (glmkv_launch_shape cannot give it without K)
+                drv.launch("glm_quant", (T * ((K + 511) // 512) + 7) // 8, 256, 0, args)
+            torch.cuda.synchronize()
+            outs.append([y.cpu().numpy() for y in (q, sf)])
+        for a, b in zip(*outs):
+            assert np.array_equal(a, b), "quant"
     finally:
         drv.close()
