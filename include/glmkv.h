@@ -115,9 +115,24 @@ int glmkv_add_rms_quant(const void* a, void* res, const void* gamma, void* norme
  * Needs K % 128 == 0, ldx >= K, ldx % 8 == 0, x and q 16-byte aligned, sf 4, sf_rows >= T. */
 int glmkv_quant(const void* x, int ldx, void* q, void* sf, int sf_rows, int K, int T, glmkv_stream_t stream);
 
+/* The indexer's fp8 MQA logits read straight from the indexer cache pages (the gather-free input
+ * format): for each row r < R and key position p < klen[r] of its sequence row_seq[r],
+ *   logits[r * stride + p] = sum_h w[r][h] * relu(sum_d iq[r][h][d] * key[p][d]) * scale[p],
+ * key / scale at page block_table[row_seq[r] * max_pages + p / 64], row p % 64 of `idx` (n_pages
+ * pages of 8448 B). Positions p >= klen[r] (or >= stride) are not written.
+ * Replaces ops `idx_gather` plus the indexer's MQA launch (kern-glm53 scripts/gen.py:124-126,
+ * scripts/glm_ops.py:104-134: DeepGEMM's sm100 fp8 MQA logits on the gathered kg / ksf, compressed
+ * layout). iq [R, 32, 128] e4m3 and w [R, 32] f32 are glm_q_post's iq and wout; row_seq and klen come
+ * from glm_plan. Runs on the tensor cores (tcgen05, kind::f8f6f4). Needs iq, idx and w 16-byte aligned,
+ * logits 4-byte aligned, stride >= every klen. */
+int glmkv_mqa_logits_paged(const void* iq, const void* idx, int n_pages, const int32_t* block_table, int max_pages,
+                           const int32_t* row_seq, const int32_t* klen, const float* w, float* logits, int stride,
+                           int R, glmkv_stream_t stream);
+
 /* The launch shape (grid x, block x, dynamic shared memory bytes) libglmkv uses for the kernel
  * `entry` ("glm_plan", "glm_mla_prep", "glm_mla_prep_fp8", "glm_idx_gather", "glm_kv_dequant",
- * "glm_topk_stream", "glm_topk_slots", "glm_q_post", "glm_add_rms_quant") on the current device for a call of T fresh rows: what a kern
+ * "glm_topk_stream", "glm_topk_slots", "glm_q_post", "glm_add_rms_quant", "glm_mqa_logits_paged") on
+ * the current device for a call of T fresh rows: what a kern
  * manifest's `impl.launches` entry for the cubin must use. The persistent page kernels depend on the
  * device's SM count only. No counterpart in the reference, whose shapes are fixed in its manifest
  * generator (kern-glm53 scripts/gen.py:95-135, 172-177). */

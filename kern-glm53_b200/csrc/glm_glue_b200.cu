@@ -2,3 +2,4 @@
 // kern-glm53 glue entry names and parameter lists, for a kern manifest. Launch shapes are listed
 // beside each entry in glmkv_kernels.cuh.
 #include "glmkv_kernels.cuh"
+#include "glmkv_mqa.cuh"

@@ -8,8 +8,11 @@
 #include <cstring>
 #include <mutex>
 
+#include <cudaTypedefs.h>
+
 #include "glmkv.h"
 #include "glmkv_kernels.cuh"
+#include "glmkv_mqa.cuh"
 
 #define GLMKV_API extern "C" __attribute__((visibility("default")))
 
@@ -28,6 +31,7 @@ struct DeviceInfo {
   int ga_ctas = 0;    // resident gather CTAs an SM
   int prep_ctas = 0;  // resident append CTAs an SM
   int arq_ctas = 0;   // resident add_rms_quant CTAs an SM
+  int mq_ctas = 0;    // resident MQA logits CTAs an SM
 };
 
 std::once_flag g_once[MAX_DEVICES];
@@ -59,7 +63,12 @@ const DeviceInfo* device_info() {
                    cudaSuccess;
     ok = ok && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.arq_ctas, glm_add_rms_quant, ARQ_THREADS, ARQ_SMEM) ==
                    cudaSuccess;
-    if (!ok || d.sms <= 0 || d.dq_ctas <= 0 || d.ga_ctas <= 0 || d.prep_ctas <= 0 || d.arq_ctas <= 0) {
+    ok = ok && cudaFuncSetAttribute(glm_mqa_logits_paged, cudaFuncAttributeMaxDynamicSharedMemorySize, MQ_SMEM) ==
+                   cudaSuccess;
+    ok = ok && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.mq_ctas, glm_mqa_logits_paged, MQ_THREADS, MQ_SMEM) ==
+                   cudaSuccess;
+    if (!ok || d.sms <= 0 || d.dq_ctas <= 0 || d.ga_ctas <= 0 || d.prep_ctas <= 0 || d.arq_ctas <= 0 ||
+        d.mq_ctas <= 0) {
       d.status = GLMKV_ERR_DEVICE;
       cudaGetLastError();
     }
@@ -117,6 +126,21 @@ int prep(const void* x, int lda, const void* g_q, const void* g_kv, const void* 
   return launch(FP8 ? glm_mla_prep_fp8 : glm_mla_prep, grid, PREP_THREADS, PREP_SMEM, stream, (const bf16*)x, lda,
                 (const bf16*)g_q, (const bf16*)g_kv, (const bf16*)rope, pos, (const long long*)slot, (u8*)kv, (u8*)idx,
                 (const bf16*)ik_w, (const bf16*)ik_b, (u8*)qq, (u8*)qsf, sf_rows, T);
+}
+
+// cuTensorMapEncodeTiled, from the driver through the runtime (no link against libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      f = nullptr;
+    }
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
 }
 
 }  // namespace
@@ -222,6 +246,39 @@ GLMKV_API int glmkv_quant(const void* x, int ldx, void* q, void* sf, int sf_rows
   return launch(glm_quant, (int)grid, QT_THREADS, 0, stream, (const bf16*)x, ldx, (u8*)q, (u8*)sf, sf_rows, K, T);
 }
 
+GLMKV_API int glmkv_mqa_logits_paged(const void* iq, const void* idx, int n_pages, const int32_t* block_table,
+                                     int max_pages, const int32_t* row_seq, const int32_t* klen, const float* w,
+                                     float* logits, int stride, int R, glmkv_stream_t stream) {
+  if (R < 0 || n_pages < 1 || max_pages < 1 || stride < 1) return GLMKV_ERR_ARG;
+  if (R == 0) return GLMKV_OK;
+  if (!iq || !idx || !block_table || !row_seq || !klen || !w || !logits) return GLMKV_ERR_ARG;
+  if ((long long)R * IH > 0xffffffffll) return GLMKV_ERR_ARG;
+  if (!aligned(iq, 16) || !aligned(idx, 16) || !aligned(w, 16) || !aligned(logits, 4)) return GLMKV_ERR_ALIGN;
+  const DeviceInfo* d = device_info();
+  if (!d) return GLMKV_ERR_DEVICE;
+  const auto encode = tensor_map_encoder();
+  if (!encode) return GLMKV_ERR_DEVICE;
+  // iq as [R * 32 rows][128 B]; a box is one block of 8 rows (256 rows), 128-byte swizzle
+  CUtensorMap tm_q, tm_k;
+  const cuuint64_t q_dims[2] = {(cuuint64_t)ID, (cuuint64_t)R * IH}, q_strides[1] = {(cuuint64_t)ID};
+  const cuuint32_t q_box[2] = {(cuuint32_t)ID, (cuuint32_t)MQ_N}, ones[3] = {1, 1, 1};
+  if (encode(&tm_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(iq), q_dims, q_strides, q_box, ones,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return GLMKV_ERR_ARG;
+  // the indexer cache as [pages][64 rows][128 B], page stride 8448 B; a box is one page's keys
+  const cuuint64_t k_dims[3] = {(cuuint64_t)ID, (cuuint64_t)PAGE, (cuuint64_t)n_pages};
+  const cuuint64_t k_strides[2] = {(cuuint64_t)ID, (cuuint64_t)IDX_PAGE};
+  const cuuint32_t k_box[3] = {(cuuint32_t)ID, (cuuint32_t)PAGE, 1};
+  if (encode(&tm_k, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(idx), k_dims, k_strides, k_box, ones,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return GLMKV_ERR_ARG;
+  const int grid = std::min(d->sms * d->mq_ctas, (R + MQ_ROWS - 1) / MQ_ROWS);
+  return launch(glm_mqa_logits_paged, grid, MQ_THREADS, MQ_SMEM, stream, tm_q, tm_k, (const u8*)idx, n_pages,
+                block_table, max_pages, row_seq, klen, w, logits, stride, R);
+}
+
 GLMKV_API int glmkv_launch_shape(const char* entry, int T, int* grid, int* block, int* smem_bytes) {
   if (!entry || !grid || !block || !smem_bytes || T < 0) return GLMKV_ERR_ARG;
   const auto is = [entry](const char* s) { return strcmp(entry, s) == 0; };
@@ -233,6 +290,11 @@ GLMKV_API int glmkv_launch_shape(const char* entry, int T, int* grid, int* block
     const DeviceInfo* d = device_info();
     if (!d) return GLMKV_ERR_DEVICE;
     *grid = std::min(d->sms * d->arq_ctas, std::max(T, 1)), *block = ARQ_THREADS, *smem_bytes = ARQ_SMEM;
+  } else if (is("glm_mqa_logits_paged")) {
+    const DeviceInfo* d = device_info();
+    if (!d) return GLMKV_ERR_DEVICE;
+    *grid = std::min(d->sms * d->mq_ctas, std::max((T + MQ_ROWS - 1) / MQ_ROWS, 1)), *block = MQ_THREADS,
+    *smem_bytes = MQ_SMEM;
   } else if (is("glm_q_post")) {
     *grid = (T + QP_WARPS - 1) / QP_WARPS, *block = QP_THREADS, *smem_bytes = 0;
   } else if (is("glm_topk_stream") || is("glm_topk_slots")) {

@@ -1,0 +1,401 @@
+// The indexer's fp8 MQA logits read straight from the page-blocked indexer cache: the gather-free
+// input format (the row after glm_idx_gather in kern-glm53's indexer, scripts/glm_ops.py:104-134).
+//
+//   logits[r * stride + p] = sum_h w[r, h] * relu( sum_d q[r, h, d] * k[p, d] ) * s[p]
+//
+// for every key position p < klen[r] of row r's sequence (row_seq[r]); q the e4m3 indexer query
+// [R, 32, 128] (glm_q_post), w its head weights [R, 32] f32 (scale folded in), k / s the e4m3 key and
+// f32 scale of position p: page block_table[seq][p / 64], row p % 64 of the indexer cache. This is
+// the definition DeepGEMM's fp8_mqa_logits is tested against, in its compressed layout (row r's
+// logits at [r][0, ke - ks)); the scale is non-negative, so relu(dot * s) = relu(dot) * s.
+//
+// One CTA per SM, warp-specialised, on Blackwell's tensor cores:
+//  - warp 0 (one lane): bulk tensor copies (TMA, 128-byte swizzle) of a block of 8 query rows
+//    (256 (row, head) rows of 128 bytes) and of key tiles (two 64-key pages, straight from the cache)
+//    into a ring of shared-memory stages;
+//  - warp 1: allocates 512 TMEM columns; one lane issues tcgen05.mma kind::f8f6f4 (e4m3 x e4m3 -> f32),
+//    M = 128 keys x N = 256 (row, head) x K = 128 (four K = 32 steps) into one of two TMEM
+//    accumulators, and commits each stage and accumulator back to its barrier;
+//  - warps 2..9: the epilogue. Warp w reads TMEM lanes 32 (w % 4) .. + 31 (one key a thread) and half
+//    of the columns (four query rows), then relu, the head-weighted sum and the key's scale, and
+//    stores the logit (32 consecutive keys a warp: 128-byte coalesced rows).
+// A block of rows that spans two sequences is worked as two segments over the same query stage.
+// Every wait is bounded; a wait that gives up sets the fault word, stops every role, waits for the
+// copies and MMAs in flight and frees TMEM before returning.
+#pragma once
+
+#include <cuda.h>
+
+#include "glmkv_kernels.cuh"
+
+namespace glmkv {
+
+constexpr int MQ_ROWS = 8;                       // query rows a block: N = 8 x 32 heads
+constexpr int MQ_N = MQ_ROWS * IH;               // 256 (row, head) rows
+constexpr int MQ_KEYS = 2 * PAGE;                // keys a tile (M): two cache pages
+constexpr int MQ_CHUNK = 16;                     // key tiles a work item (2048 keys)
+constexpr int MQ_KSTAGES = 6;
+constexpr int MQ_QBYTES = MQ_N * ID;             // 32,768 B: a query block, e4m3
+constexpr int MQ_KBYTES = MQ_KEYS * ID;          // 16,384 B: a key tile, e4m3
+constexpr int MQ_SCBYTES = MQ_KEYS * 4;          // 512 B: its keys' f32 scales
+constexpr int MQ_EPI_WARPS = 16;                 // four a TMEM lane quarter, two query rows each
+constexpr int MQ_THREADS = 32 * (2 + MQ_EPI_WARPS);
+constexpr int MQ_TMEM_COLS = 2 * MQ_N;           // two f32 accumulators of 256 columns
+constexpr int MQ_WBYTES = MQ_EPI_WARPS * 2 * IH * 4;  // each epilogue warp's two rows of head weights
+constexpr int MQ_SMEM = 1024 + 2 * MQ_QBYTES + MQ_KSTAGES * (MQ_KBYTES + MQ_SCBYTES) + MQ_WBYTES;  // + 1 KB: align
+// instruction descriptor, kind::f8f6f4: D f32 (bits 4-5 = 1), A and B e4m3 (0), both K-major (0),
+// N >> 3 at bits 17-22, M >> 4 at bits 24-28
+constexpr uint32_t MQ_IDESC = (1u << 4) | ((uint32_t)(MQ_N >> 3) << 17) | ((uint32_t)(MQ_KEYS >> 4) << 24);
+
+// Shared-memory matrix descriptor of a K-major operand in the 128-byte swizzle layout: rows of 128
+// bytes, 8-row groups 1024 bytes apart (SBO), the tile 1024-byte aligned (base offset 0). Start
+// address bits 0-13 (>> 4), LBO bits 16-29 (unused for this layout: 16 B), SBO bits 32-45, version 1
+// at bits 46-47, layout 2 (128-byte swizzle) at bits 61-63. A K step of 32 bytes adds 2 to the start.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// The barrier's phase completes once every tcgen05 operation this thread issued before has.
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// 32 f32 columns of this warp's 32 TMEM lanes (one lane a thread) at `taddr`, then wait for them.
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// try_wait with a suspend-time hint: the warp sleeps until the phase completes (or `hint_ns` pass)
+// instead of spinning, so waiting warps leave the issue slots to the working ones.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+// A bounded wait that also gives up as soon as another role has (the CTA's abort word is set).
+__device__ __forceinline__ bool mq_wait(uint32_t bar, uint32_t parity, const volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
+    if (*abort) return false;
+    if (global_ns() - t0 > WAIT_LIMIT_NS) return false;
+  }
+  return true;
+}
+
+// The work of a launch is a grid of items (query block qb of 8 rows, key chunk c of 16 tiles = 2048
+// positions), item i = qb * nch + c going to CTA i % G. An item covers, in each segment of its block
+// (a run of rows of one sequence), the key tiles c * 16 .. c * 16 + 15 below the segment's largest
+// klen; an item with none is skipped by every role alike. Every role walks the items in this order.
+struct MqSegment {
+  int sb, se, seq, kmax, kb0, kb1;  // rows [sb, se), key tiles [kb0, kb1)
+};
+// f(segment) for each segment of block qb with key tiles in chunk c; false as soon as f returns false.
+template <class F>
+__device__ __forceinline__ bool mq_segments(const int* __restrict__ row_seq, const int* __restrict__ klen, int R, int qb,
+                                            int c, F&& f) {
+  const int r0 = qb * MQ_ROWS, re = min(r0 + MQ_ROWS, R);
+  for (int sb = r0; sb < re;) {
+    const int s = row_seq[sb];
+    int se = sb + 1, kmax = klen[sb];
+    while (se < re && row_seq[se] == s) kmax = max(kmax, klen[se++]);
+    const int nkb = (kmax + MQ_KEYS - 1) / MQ_KEYS;
+    const int kb0 = c * MQ_CHUNK, kb1 = min(kb0 + MQ_CHUNK, nkb);
+    if (kb0 < kb1 && !f(MqSegment{sb, se, s, kmax, kb0, kb1})) return false;
+    sb = se;
+  }
+  return true;
+}
+__device__ __forceinline__ bool mq_item_has_tiles(const int* __restrict__ row_seq, const int* __restrict__ klen, int R,
+                                                  int qb, int c) {
+  bool any = false;
+  mq_segments(row_seq, klen, R, qb, c, [&](const MqSegment&) {
+    any = true;
+    return false;  // one is enough
+  });
+  return any;
+}
+
+__device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const u8* __restrict__ idx,
+                                          int n_pages, const int* __restrict__ block_table, int max_pages,
+                                          const int* __restrict__ row_seq, const int* __restrict__ klen,
+                                          const float* __restrict__ w, float* __restrict__ logits, int stride, int R) {
+  extern __shared__ __align__(1024) u8 mq_smem_raw[];
+  __shared__ __align__(8) unsigned long long q_full[2], q_empty[2], k_full[MQ_KSTAGES], k_empty[MQ_KSTAGES],
+      acc_full[2], acc_empty[2], mma_done;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, l = tid & 31;
+  const uint32_t sbase = (smem_u32(mq_smem_raw) + 1023u) & ~1023u;  // 1024-aligned for the swizzle
+  const uint32_t qbuf = sbase, kbuf = sbase + 2 * MQ_QBYTES, scbuf = kbuf + MQ_KSTAGES * MQ_KBYTES;
+  const uint32_t wbuf = scbuf + MQ_KSTAGES * MQ_SCBYTES;
+  u8* const sgen = mq_smem_raw + (sbase - smem_u32(mq_smem_raw));  // generic pointer of sbase
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&q_full[i]), 1);
+      mbar_init(smem_u32(&q_empty[i]), 1);
+      mbar_init(smem_u32(&acc_full[i]), 1);
+      mbar_init(smem_u32(&acc_empty[i]), MQ_EPI_WARPS);
+    }
+    for (int i = 0; i < MQ_KSTAGES; ++i) {
+      mbar_init(smem_u32(&k_full[i]), 1);
+      mbar_init(smem_u32(&k_empty[i]), 1 + MQ_EPI_WARPS);  // the MMAs, and every epilogue warp's scale read
+    }
+    mbar_init(smem_u32(&mma_done), 1);
+    mbar_init_fence();
+    abort_flag = 0;
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(MQ_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  pdl_trigger();  // one CTA per SM, all resident
+  pdl_wait();
+  const volatile int* abort = &abort_flag;
+  auto give_up = [&]() {
+    atomicOr(&g_fault, FAULT_WAIT_TIMEOUT);
+    abort_flag = 1;
+  };
+  const int nqb = (R + MQ_ROWS - 1) / MQ_ROWS, nch = ((stride + MQ_KEYS - 1) / MQ_KEYS + MQ_CHUNK - 1) / MQ_CHUNK;
+  const long long items = (long long)nqb * nch;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer: bulk tensor copies
+    uint32_t kit = 0, qit = 0, k_issued = 0;
+    int q_issued = 0;
+    bool ok = true;
+    for (long long i = blockIdx.x; ok && i < items; i += gridDim.x) {
+      const int qb = (int)(i / nch), c = (int)(i % nch);
+      if (!mq_item_has_tiles(row_seq, klen, R, qb, c)) continue;
+      const int qs = qit & 1;
+      if (l == 0) {
+        ok = mq_wait(smem_u32(&q_empty[qs]), ((qit >> 1) & 1) ^ 1, abort);
+        if (ok) {
+          mbar_arrive_expect_tx(smem_u32(&q_full[qs]), MQ_QBYTES);
+          tma_load_2d(qbuf + qs * MQ_QBYTES, tm_q, 0, qb * MQ_ROWS * IH, smem_u32(&q_full[qs]));
+        }
+      }
+      ok = __shfl_sync(FULL, ok, 0);
+      if (!ok) break;
+      q_issued |= 1 << qs;
+      ++qit;
+      ok = mq_segments(row_seq, klen, R, qb, c, [&](const MqSegment& g) {
+        // lane j holds the page of position block 2 kb0 + j (the item's up to 32 pages)
+        const int pj = 2 * g.kb0 + l;
+        int pg = -1;
+        if (pj * PAGE < g.kmax && pj < max_pages) {
+          pg = block_table[(size_t)g.seq * max_pages + pj];
+          if (pg >= n_pages) pg = -1;
+          if (pg < 0) atomicOr(&g_fault, FAULT_BAD_PAGE);
+        }
+        for (int kb = g.kb0; kb < g.kb1; ++kb) {
+          const int st = kit % MQ_KSTAGES;
+          const int p0 = __shfl_sync(FULL, pg, 2 * (kb - g.kb0)), p1 = __shfl_sync(FULL, pg, 2 * (kb - g.kb0) + 1);
+          bool okk = true;
+          if (l == 0) {
+            okk = mq_wait(smem_u32(&k_empty[st]), ((kit / MQ_KSTAGES) & 1) ^ 1, abort);
+            if (okk) {
+              const uint32_t bytes = (p0 >= 0 ? MQ_KBYTES / 2 + MQ_SCBYTES / 2 : 0) +
+                                     (p1 >= 0 ? MQ_KBYTES / 2 + MQ_SCBYTES / 2 : 0);
+              mbar_arrive_expect_tx(smem_u32(&k_full[st]), bytes);
+              const int pp[2] = {p0, p1};
+#pragma unroll
+              for (int j = 0; j < 2; ++j)
+                if (pp[j] >= 0) {
+                  tma_load_3d(kbuf + st * MQ_KBYTES + j * (MQ_KBYTES / 2), tm_k, 0, 0, pp[j], smem_u32(&k_full[st]));
+                  tma_load_1d(scbuf + st * MQ_SCBYTES + j * (MQ_SCBYTES / 2),
+                              idx + (size_t)pp[j] * IDX_PAGE + PAGE * ID, MQ_SCBYTES / 2, smem_u32(&k_full[st]));
+                }
+            }
+          }
+          if (!__shfl_sync(FULL, okk, 0)) return false;
+          k_issued |= 1u << st;
+          ++kit;
+        }
+        return true;
+      });
+    }
+    if (!ok && l == 0) give_up();
+    if (l == 0) {  // wait (bounded) for every copy still in flight: the last phase of each stage used
+      for (int st = 0; st < MQ_KSTAGES; ++st)
+        if (k_issued & (1u << st)) {
+          const uint32_t last = (kit - 1 - ((kit - 1 - st) % MQ_KSTAGES)) / MQ_KSTAGES;  // index of its last use
+          mbar_wait_bounded(smem_u32(&k_full[st]), last & 1, WAIT_LIMIT_NS);
+        }
+      for (int qs = 0; qs < 2; ++qs)
+        if (q_issued & (1 << qs)) {
+          const uint32_t last = (qit - 1 - ((qit - 1 - qs) & 1)) >> 1;  // index of its last use
+          mbar_wait_bounded(smem_u32(&q_full[qs]), last & 1, WAIT_LIMIT_NS);
+        }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issue (one lane)
+    if (l == 0) {
+      uint32_t kit = 0, qit = 0;
+      bool ok = true, issued = false;
+      for (long long i = blockIdx.x; ok && i < items; i += gridDim.x) {
+        const int qb = (int)(i / nch), c = (int)(i % nch);
+        if (!mq_item_has_tiles(row_seq, klen, R, qb, c)) continue;
+        const int qs = qit & 1;
+        if (!(ok = mq_wait(smem_u32(&q_full[qs]), (qit >> 1) & 1, abort))) break;
+        const uint64_t bdesc = sw128_desc(qbuf + qs * MQ_QBYTES);
+        ok = mq_segments(row_seq, klen, R, qb, c, [&](const MqSegment& g) {
+          for (int kb = g.kb0; kb < g.kb1; ++kb) {
+            const int st = kit % MQ_KSTAGES, a = kit & 1;
+            if (!mq_wait(smem_u32(&k_full[st]), (kit / MQ_KSTAGES) & 1, abort)) return false;
+            if (!mq_wait(smem_u32(&acc_empty[a]), ((kit >> 1) & 1) ^ 1, abort)) return false;
+            tc_fence_after();
+            const uint64_t adesc = sw128_desc(kbuf + st * MQ_KBYTES);
+#pragma unroll
+            for (int kk = 0; kk < ID / 32; ++kk)
+              tc_mma(tmem + a * MQ_N, adesc + 2 * kk, bdesc + 2 * kk, MQ_IDESC, kk > 0);
+            issued = true;
+            tc_commit(smem_u32(&k_empty[st]));
+            tc_commit(smem_u32(&acc_full[a]));
+            ++kit;
+          }
+          return true;
+        });
+        if (ok) tc_commit(smem_u32(&q_empty[qs]));
+        ++qit;
+      }
+      if (!ok) give_up();
+      if (issued) {  // every MMA has completed before TMEM is freed
+        tc_commit(smem_u32(&mma_done));
+        mbar_wait_bounded(smem_u32(&mma_done), 0, WAIT_LIMIT_NS);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue: TMEM -> logits
+    const int qd = warp & 3, cq = (warp - 2) >> 2;  // TMEM lane quarter; query rows 2 cq, 2 cq + 1 of a block
+    float* wsm = reinterpret_cast<float*>(sgen + (wbuf - sbase)) + (warp - 2) * 2 * IH;
+    uint32_t kit = 0;
+    bool ok = true;
+    for (long long i = blockIdx.x; ok && i < items; i += gridDim.x) {
+      const int qb = (int)(i / nch), c = (int)(i % nch);
+      if (!mq_item_has_tiles(row_seq, klen, R, qb, c)) continue;
+      const int ra = qb * MQ_ROWS + 2 * cq;  // this warp's rows ra, ra + 1
+      // their head weights (zero past R), interleaved by head into the warp's shared-memory slice:
+      // wsm[2 h + j] = w[ra + j][h], so one packed FMA takes head h of both rows
+      __syncwarp();
+      {
+        const int j = l >> 4, h2 = 2 * (l & 15);
+        const int r = ra + j;
+        const float2 v = r < R ? __ldg(reinterpret_cast<const float2*>(w + (size_t)r * IH + h2)) : make_float2(0.f, 0.f);
+        wsm[2 * h2 + j] = v.x;
+        wsm[2 * h2 + 2 + j] = v.y;
+      }
+      __syncwarp();
+      const int kl0 = ra < R ? klen[ra] : 0, kl1 = ra + 1 < R ? klen[ra + 1] : 0;
+      ok = mq_segments(row_seq, klen, R, qb, c, [&](const MqSegment& g) {
+        const bool live0 = ra >= g.sb && ra < g.se, live1 = ra + 1 >= g.sb && ra + 1 < g.se;
+        for (int kb = g.kb0; kb < g.kb1; ++kb) {
+          const int st = kit % MQ_KSTAGES, a = kit & 1;
+          const bool okw = mq_wait(smem_u32(&acc_full[a]), (kit >> 1) & 1, abort);
+          if (__any_sync(FULL, !okw)) return false;  // the warp leaves together: tcgen05.ld is warp-collective
+          tc_fence_after();
+          const int p = kb * MQ_KEYS + 32 * qd + l;  // this thread's key position
+          const float scale = reinterpret_cast<const float*>(sgen + (scbuf - sbase) + st * MQ_SCBYTES)[32 * qd + l];
+          __syncwarp();
+          if (l == 0) mbar_arrive(smem_u32(&k_empty[st]));  // the stage's scales are read
+          if (live0 || live1) {
+            float v[2][32];
+            tc_ld32(tmem + a * MQ_N + ((uint32_t)(32 * qd) << 16) + 2 * cq * IH, v[0]);
+            tc_ld32(tmem + a * MQ_N + ((uint32_t)(32 * qd) << 16) + (2 * cq + 1) * IH, v[1]);
+            // sum over heads of w * relu(v) for both rows at once: two chains of packed FMAs (even and
+            // odd heads), each lane holding (row ra, row ra + 1)
+            float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int h = 0; h < IH; h += 2) {
+              const float4 ww = *reinterpret_cast<const float4*>(wsm + 2 * h);  // w[ra][h], w[ra+1][h], .. h + 1
+              acc0 = fma2(make_float2(ww.x, ww.y), make_float2(fmaxf(v[0][h], 0.f), fmaxf(v[1][h], 0.f)), acc0);
+              acc1 = fma2(make_float2(ww.z, ww.w), make_float2(fmaxf(v[0][h + 1], 0.f), fmaxf(v[1][h + 1], 0.f)), acc1);
+            }
+            const float2 sum = make_float2(__fadd_rn(acc0.x, acc1.x), __fadd_rn(acc0.y, acc1.y));
+            if (p < stride) {
+              if (live0 && p < kl0) logits[(size_t)ra * stride + p] = __fmul_rn(sum.x, scale);
+              if (live1 && p < kl1) logits[(size_t)(ra + 1) * stride + p] = __fmul_rn(sum.y, scale);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (l == 0) mbar_arrive(smem_u32(&acc_empty[a]));
+          ++kit;
+        }
+        return true;
+      });
+    }
+    if (!ok && l == 0) give_up();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(MQ_TMEM_COLS) : "memory");
+  }
+}
+
+}  // namespace glmkv
+
+// The indexer's MQA logits of rows 0 .. R - 1 over their sequences' keys, read from the indexer
+// cache pages (no gather). tm_q maps iq as [R * 32 rows][128 B] (box 256 rows, 128-byte swizzle);
+// tm_k maps the indexer cache as [pages][64 rows][128 B] with strides 8448 and 128 B (box one page,
+// 128-byte swizzle). idx is the same cache of n_pages pages (the key scales at each page's tail);
+// a block-table entry outside 0 .. n_pages - 1 is skipped and flagged. No counterpart
+// among the glue kernels: it replaces the gather plus DeepGEMM's MQA logits.
+//   persistent: grid = SMs, block 576, dynamic smem MQ_SMEM (172,032 B)
+extern "C" __global__ void __launch_bounds__(glmkv::MQ_THREADS, 1)
+    glm_mqa_logits_paged(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                         const glmkv::u8* __restrict__ idx, int n_pages, const int* __restrict__ block_table,
+                         int max_pages,
+                         const int* __restrict__ row_seq, const int* __restrict__ klen, const float* __restrict__ w,
+                         float* __restrict__ logits, int stride, int R) {
+  glmkv::mq_logits(&tm_q, &tm_k, idx, n_pages, block_table, max_pages, row_seq, klen, w, logits, stride, R);
+}

@@ -22,6 +22,7 @@ SIGNATURES = {
     "glmkv_q_post": [P, I, P, P, P, P, P, P, I, I, P],
     "glmkv_add_rms_quant": [P, P, P, P, P, P, I, I, P],
     "glmkv_quant": [P, I, P, P, I, I, I, P],
+    "glmkv_mqa_logits_paged": [P, P, I, P, I, P, P, P, P, I, I, P],
     "glmkv_launch_shape": [ctypes.c_char_p, I, P, P, P],
     "glmkv_selftest_wait": [ctypes.c_uint64, P, P],
     "glmkv_fault_flags": [P, I],

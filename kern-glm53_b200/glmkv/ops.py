@@ -24,6 +24,10 @@ by the op's scalars, exactly in the manifest's parameter order, and enqueues one
     rms_quant        the same without a (nulled, 171)                      glm_add_rms_quant
     head_norm        the same without q, sf (nulled, 156-158)              glm_add_rms_quant
     quant_o          x, ldx, q, sf, sf_rows, K, T         (103-105)        glm_quant
+    mqa_logits_paged iq, idx, n_pages, block_table, max_pages, row_seq,  glm_mqa_logits_paged
+                     klen, w, logits, stride, R: the indexer's MQA logits
+                     from the cache pages (replaces idx_gather + the MQA
+                     launch of indexer.<j>, glm_ops.py:104-134)
 
 Errors (null or misaligned buffers, sizes out of range, a failed launch) raise ``GlmKvError``.
 """
@@ -147,3 +151,12 @@ def quant_o(x, ldx, q, sf, sf_rows, K, T, stream=None):
     """x [T, K] e4m3 per 128 columns with packed UE8M0 scales (op `quant_o`)."""
     _lib.call("glmkv_quant", _ptr(x, "bf16", "x"), int(ldx), _ptr(q, "u8", "q"), _ptr(sf, "u8", "sf"), int(sf_rows),
               int(K), int(T), _stream(stream))
+
+
+def mqa_logits_paged(iq, idx, n_pages, block_table, max_pages, row_seq, klen, w, logits, stride, R, stream=None):
+    """The indexer's fp8 MQA logits read from the indexer cache pages, on the tensor cores
+    (op `mqa_logits_paged`): logits[r, p] for p < klen[r], row r's sequence row_seq[r]."""
+    _lib.call("glmkv_mqa_logits_paged", _ptr(iq, "u8", "iq"), _ptr(idx, "u8", "idx"), int(n_pages),
+              _ptr(block_table, "i32", "block_table"), int(max_pages), _ptr(row_seq, "i32", "row_seq"),
+              _ptr(klen, "i32", "klen"), _ptr(w, "f32", "w"), _ptr(logits, "f32", "logits"), int(stride), int(R),
+              _stream(stream))

@@ -1,0 +1,97 @@
+"""glm_mqa_logits_paged, the indexer's fp8 MQA logits read straight from the indexer cache pages,
+against the NumPy restatement of DeepGEMM's published fp8_mqa_logits (oracle/mqa.py).
+
+DeepGEMM is absent from kern-glm53 (an empty submodule), so the oracle is the formula its tests use;
+the dot products there are exact (float64), and the device's f32 tensor-core result must lie within
+2^-14 of `magnitude` (the same sum over |.|) of it. Positions at or past a row's klen are not written.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+TOL = 2.0 ** -14
+
+
+def _codes(rng, n):
+    """e4m3 codes without the NaN codes (0x7F, 0xFF): what the append's satfinite conversion writes."""
+    c = rng.integers(0, 256, size=n, dtype=np.uint8)
+    return np.where((c & 0x7F) == 0x7F, c - 1, c).astype(np.uint8)
+
+
+def _case(prefix, fresh, seed):
+    from glmkv import workload as W
+
+    rng = np.random.default_rng(seed)
+    call = W.make_call(prefix, fresh, rng, spare_pages=2)
+    pool = np.empty((call.n_pages, 64 * 132), np.uint8)
+    pool[:, :8192] = _codes(rng, call.n_pages * 8192).reshape(call.n_pages, 8192)
+    pool[:, 8192:] = np.exp2(rng.integers(-12, 4, size=(call.n_pages, 64))).astype(np.float32).view(np.uint8)
+    R = call.T
+    iq = _codes(rng, R * 32 * 128)
+    w = rng.standard_normal((R, 32)).astype(np.float32)
+    row_seq = np.repeat(np.arange(call.nseq, dtype=np.int32), call.fresh)
+    klen = W.positions(call) + 1
+    return call, pool.reshape(-1), iq, w, row_seq, klen.astype(np.int32)
+
+
+def _run(cuda, call, pool, iq, w, row_seq, klen, stride):
+    import glmkv
+
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    R = len(row_seq)
+    logits = torch.full((R * stride,), float("nan"), dtype=torch.float32, device=cuda)
+    glmkv.mqa_logits_paged(t(iq), t(pool), call.n_pages, t(call.block_table), call.max_pages, t(row_seq), t(klen),
+                           t(w), logits, stride, R)
+    torch.cuda.synchronize()
+    assert glmkv.fault_flags() == 0
+    return logits.cpu().numpy().reshape(R, stride)
+
+
+def _check(got, call, pool, iq, w, row_seq, klen, what):
+    from oracle import mqa
+
+    want = mqa.mqa_logits_paged(iq, pool, call.block_table, call.max_pages, row_seq, klen, w)
+    worst = 0.0
+    for r, (lg, mg) in enumerate(want):
+        k = int(klen[r])
+        g = got[r, :k].astype(np.float64)
+        assert np.all(np.isfinite(g)), f"{what}: row {r} has non-finite logits"
+        err = np.abs(g - lg) / np.maximum(mg, 1e-30)
+        worst = max(worst, float(err.max()))
+        assert err.max() <= TOL, f"{what}: row {r} position {int(err.argmax())}: {g[err.argmax()]} vs {lg[err.argmax()]}"
+        assert np.all(np.isnan(got[r, k:])), f"{what}: row {r} wrote past klen"
+    print(f"{what}: worst error {worst:.3g} of magnitude")
+
+
+def test_mqa_logits_small_ragged(cuda):
+    """Four sequences whose rows straddle the 8-row blocks; key counts across the 64-key page and
+    128-key tile edges (1 .. 1509)."""
+    case = _case([100, 0, 700, 1500, 63], [20, 37, 13, 9, 1], seed=81)
+    call, pool, iq, w, row_seq, klen = case
+    stride = int(klen.max()) + 5
+    got = _run(cuda, *case, stride)
+    _check(got, *case, "small")
+
+
+def test_mqa_logits_cfg0(cuda):
+    """cfg0 (two sequences, 1,024 rows, up to 3,584 keys a row)."""
+    from glmkv import workload as W
+
+    c0 = W.config("cfg0", seed=4)
+    case = _case(c0.prefix, c0.fresh, seed=82)
+    got = _run(cuda, *case, 4096)
+    _check(got, *case, "cfg0")
+
+
+def test_mqa_logits_rejects_bad_arguments():
+    import glmkv
+    from glmkv import _lib
+
+    L = glmkv.lib()
+    A = 0x10000
+    assert L.glmkv_mqa_logits_paged(A, A, 1, A, 1, A, A, A, A, 16, -1, None) == _lib.ERR_ARG
+    assert L.glmkv_mqa_logits_paged(A, A, 0, A, 1, A, A, A, A, 16, 8, None) == _lib.ERR_ARG
+    assert L.glmkv_mqa_logits_paged(A + 8, A, 1, A, 1, A, A, A, A, 16, 8, None) == _lib.ERR_ALIGN
+    assert L.glmkv_mqa_logits_paged(A, A, 1, A, 1, A, A, A, A, 16, 0, None) == _lib.OK
