@@ -35,6 +35,7 @@ sys.path[:0] = [str(ROOT), str(ROOT / "kern-glm53_b200")]
 METRIC = "fp8 KV append+paged dequant GB/s (% HBM peak), tokens/s at 1/2/4/8 B200"
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0  # the pool's earlier burst measurement, used when MEASURED_PEAKS.json is absent
 WORKLOADS = {
     "cfg3": "cfg3: one 16-sequence / 16,384-row prefill call through the cache path of all 78 layers, "
             "prefixes from {0, 2K, 64K, 256K}, stream <= 2^20 tokens, fp8 latent cache + indexer cache",
@@ -59,14 +60,15 @@ def parse():
     return ap.parse_args()
 
 
-def measured_peak():
+def measured_peak(key="hbm_gbs"):
+    """The pool's measured peak (`hbm_gbs` GB/s, or `bf16_tflops` TFLOP/s) and whether it was measured."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         try:
-            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+            return float(json.loads(p.read_text())[key]), "measured"
         except (KeyError, ValueError):
             pass
-    return FALLBACK_HBM_GBS, "fallback"
+    return (FALLBACK_HBM_GBS if key == "hbm_gbs" else FALLBACK_BF16_TFLOPS), "fallback"
 
 
 # ------------------------------------------------------------------------------------------ clocks
@@ -300,6 +302,52 @@ def next_rows(torch, impl, T, dev, reps=10):
     return rows
 
 
+def mqa_row(torch, impl, group, meta, call, dev, reps=3, sub=1024):
+    """The indexer's MQA logits of the call's rows over their sequences' keys, read from the first
+    indexer layer's cache pages (glm_mqa_logits_paged), in sub-chunks of `sub` rows as the manifest runs
+    the indexer (scripts/gen.py:483, --sub 1024): FLOPs = 2 x 32 heads x 128 dims x sum of klen."""
+    from glmkv import workload as W
+    from glmkv.stage import FULL
+
+    if impl != "glmkv":
+        return {"unavailable": "the reference's MQA logits kernel is DeepGEMM's, an empty submodule in kern-glm53"}
+    layers = [l for l in group.layers if l in FULL]
+    if not layers:
+        return {"unavailable": "no indexer layer in this stage"}
+    import glmkv
+    T = call.T
+    klen = W.positions(call).astype(np.int64) + 1
+    stride = int(klen.max())
+    g = torch.Generator(device=dev).manual_seed(6)
+    iq = torch.randint(0, 126, (T * 32 * 128,), dtype=torch.uint8, device=dev, generator=g)
+    w = torch.randn(T, 32, device=dev, generator=g)
+    logits = torch.empty(sub * stride, dtype=torch.float32, device=dev)
+    idx = group.idx[layers[0]]
+
+    def fn():
+        for j in range(0, T, sub):
+            glmkv.mqa_logits_paged(iq[j * 4096:], idx, call.n_pages, meta.block_table, call.max_pages,
+                                   group.row_seq[j:], group.klen[j:], w[j:], logits, stride, min(sub, T - j))
+    fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    us = s.elapsed_time(e) / reps * 1e3
+    flops = int(klen.sum()) * 32 * 128 * 2
+    peak, kind = measured_peak("bf16_tflops")
+    fp8_peak = 2 * peak
+    tf = flops / us / 1e6
+    del iq, w, logits
+    return {"rows": T, "sub_rows": sub, "keys_scored": int(klen.sum()), "us": round(us, 1), "TFLOP/s": round(tf, 1),
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
+                         "frac": round(tf / fp8_peak, 4),
+                         "peak_note": f"dense e4m3 = 2 x the {kind} bf16 GEMM rate (MEASURED_PEAKS.json bf16_tflops)"}}
+
+
 # ------------------------------------------------------------------------------------------ CPU baseline
 
 def cpu_baseline(call, layers, budget_s, seed):
@@ -524,6 +572,7 @@ def main():
                                "reference kernels (oracle/_ref) with the same host copies"}
     if not a.no_next_rows:
         line["next_rows"] = next_rows(torch, a.impl, call.T, dev)
+        line["next_rows"]["glm_mqa_logits_paged"] = mqa_row(torch, a.impl, group, meta, call, dev)
     if a.impl == "reference":
         line["cpu_baseline"] = {"value": line["value"], "unit": "GB/s", "cores": 1, "kind": "reference",
                                 "sample": "the whole workload: the reference's glue kernels (kern-glm53 "

@@ -274,7 +274,8 @@ GLMKV_API int glmkv_mqa_logits_paged(const void* iq, const void* idx, int n_page
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return GLMKV_ERR_ARG;
-  const int grid = std::min(d->sms * d->mq_ctas, (R + MQ_ROWS - 1) / MQ_ROWS);
+  const long long nch = ((stride + MQ_KEYS - 1) / MQ_KEYS + MQ_CHUNK - 1) / MQ_CHUNK;  // key chunks of a row block
+  const int grid = (int)std::min<long long>(d->sms * d->mq_ctas, (long long)((R + MQ_ROWS - 1) / MQ_ROWS) * nch);
   return launch(glm_mqa_logits_paged, grid, MQ_THREADS, MQ_SMEM, stream, tm_q, tm_k, (const u8*)idx, n_pages,
                 block_table, max_pages, row_seq, klen, w, logits, stride, R);
 }
@@ -290,11 +291,10 @@ GLMKV_API int glmkv_launch_shape(const char* entry, int T, int* grid, int* block
     const DeviceInfo* d = device_info();
     if (!d) return GLMKV_ERR_DEVICE;
     *grid = std::min(d->sms * d->arq_ctas, std::max(T, 1)), *block = ARQ_THREADS, *smem_bytes = ARQ_SMEM;
-  } else if (is("glm_mqa_logits_paged")) {
+  } else if (is("glm_mqa_logits_paged")) {  // persistent: any grid works; one CTA an SM
     const DeviceInfo* d = device_info();
     if (!d) return GLMKV_ERR_DEVICE;
-    *grid = std::min(d->sms * d->mq_ctas, std::max((T + MQ_ROWS - 1) / MQ_ROWS, 1)), *block = MQ_THREADS,
-    *smem_bytes = MQ_SMEM;
+    *grid = d->sms * d->mq_ctas, *block = MQ_THREADS, *smem_bytes = MQ_SMEM;
   } else if (is("glm_q_post")) {
     *grid = (T + QP_WARPS - 1) / QP_WARPS, *block = QP_THREADS, *smem_bytes = 0;
   } else if (is("glm_topk_stream") || is("glm_topk_slots")) {

@@ -42,6 +42,7 @@ constexpr int MQ_EPI_WARPS = 16;                 // four a TMEM lane quarter, tw
 constexpr int MQ_THREADS = 32 * (2 + MQ_EPI_WARPS);
 constexpr int MQ_TMEM_COLS = 2 * MQ_N;           // two f32 accumulators of 256 columns
 constexpr int MQ_WBYTES = MQ_EPI_WARPS * 2 * IH * 4;  // each epilogue warp's two rows of head weights
+constexpr int MQ_QTAB = 4096;                    // blocks whose largest klen is kept in shared memory
 constexpr int MQ_SMEM = 1024 + 2 * MQ_QBYTES + MQ_KSTAGES * (MQ_KBYTES + MQ_SCBYTES) + MQ_WBYTES;  // + 1 KB: align
 // instruction descriptor, kind::f8f6f4: D f32 (bits 4-5 = 1), A and B e4m3 (0), both K-major (0),
 // N >> 3 at bits 17-22, M >> 4 at bits 24-28
@@ -128,6 +129,21 @@ __device__ __forceinline__ bool mq_wait(uint32_t bar, uint32_t parity, const vol
 // positions), item i = qb * nch + c going to CTA i % G. An item covers, in each segment of its block
 // (a run of rows of one sequence), the key tiles c * 16 .. c * 16 + 15 below the segment's largest
 // klen; an item with none is skipped by every role alike. Every role walks the items in this order.
+// The items of this CTA, blockIdx.x, + G, + 2 G, ..., numbered chunk-major (i = c * nqb + qb, so the
+// first chunk of every block comes before any second chunk), as (block qb, chunk c) without a
+// division a step: G = cg * nqb + qg. The walk ends at the first chunk no row of the launch reaches.
+struct MqItems {
+  int qb, c, nqb, nch, qg, cg;
+  __device__ __forceinline__ MqItems(int nqb_, int nch_)
+      : qb((int)(blockIdx.x % nqb_)), c((int)(blockIdx.x / nqb_)), nqb(nqb_), nch(nch_),
+        qg((int)(gridDim.x % nqb_)), cg((int)(gridDim.x / nqb_)) {}
+  __device__ __forceinline__ bool valid() const { return c < nch; }
+  __device__ __forceinline__ void next() {
+    qb += qg;
+    c += cg;
+    if (qb >= nqb) qb -= nqb, ++c;
+  }
+};
 struct MqSegment {
   int sb, se, seq, kmax, kb0, kb1;  // rows [sb, se), key tiles [kb0, kb1)
 };
@@ -147,14 +163,18 @@ __device__ __forceinline__ bool mq_segments(const int* __restrict__ row_seq, con
   }
   return true;
 }
-__device__ __forceinline__ bool mq_item_has_tiles(const int* __restrict__ row_seq, const int* __restrict__ klen, int R,
-                                                  int qb, int c) {
-  bool any = false;
-  mq_segments(row_seq, klen, R, qb, c, [&](const MqSegment&) {
-    any = true;
-    return false;  // one is enough
-  });
-  return any;
+// Whether item (qb, c) has any tile: a segment has tiles in chunk c when its largest klen passes
+// c * 2048, so the item has some when the block's largest klen does. `qmax` holds every block's
+// largest klen when the launch has at most MQ_QTAB blocks; otherwise the rows are read here.
+__device__ __forceinline__ int mq_block_kmax(const int* __restrict__ klen, int R, int qb) {
+  int m = 0;
+  for (int r = qb * MQ_ROWS; r < min(qb * MQ_ROWS + MQ_ROWS, R); ++r) m = max(m, klen[r]);
+  return m;
+}
+__device__ __forceinline__ bool mq_item_has_tiles(const int* qmax, const int* __restrict__ klen, int R, int nqb, int qb,
+                                                  int c) {
+  const int m = nqb <= MQ_QTAB ? qmax[qb] : mq_block_kmax(klen, R, qb);
+  return m > c * MQ_CHUNK * MQ_KEYS;
 }
 
 __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const u8* __restrict__ idx,
@@ -166,6 +186,8 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
       acc_full[2], acc_empty[2], mma_done;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
+  __shared__ unsigned kmax_all;  // the largest klen of the launch's rows
+  __shared__ int qmax[MQ_QTAB];  // each block's largest klen (launches of at most MQ_QTAB blocks)
   const int tid = threadIdx.x, warp = tid >> 5, l = tid & 31;
   const uint32_t sbase = (smem_u32(mq_smem_raw) + 1023u) & ~1023u;  // 1024-aligned for the swizzle
   const uint32_t qbuf = sbase, kbuf = sbase + 2 * MQ_QBYTES, scbuf = kbuf + MQ_KSTAGES * MQ_KBYTES;
@@ -185,6 +207,7 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
     mbar_init(smem_u32(&mma_done), 1);
     mbar_init_fence();
     abort_flag = 0;
+    kmax_all = 0;
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
@@ -203,17 +226,38 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
     atomicOr(&g_fault, FAULT_WAIT_TIMEOUT);
     abort_flag = 1;
   };
-  const int nqb = (R + MQ_ROWS - 1) / MQ_ROWS, nch = ((stride + MQ_KEYS - 1) / MQ_KEYS + MQ_CHUNK - 1) / MQ_CHUNK;
-  const long long items = (long long)nqb * nch;
+  const int nqb = (R + MQ_ROWS - 1) / MQ_ROWS;
+  {  // every block's largest klen, and the launch's: the chunks any row needs (stride bounds the stores)
+    unsigned m = 0;
+    if (nqb <= MQ_QTAB) {
+      // one row a thread (rows of a block in 8 consecutive lanes), the block's max over those lanes
+      for (int r0 = 0; r0 < R; r0 += MQ_THREADS) {
+        const int r = r0 + tid;
+        unsigned k = r < R ? (unsigned)max(klen[r], 0) : 0u;
+        k = max(k, __shfl_xor_sync(FULL, k, 1));
+        k = max(k, __shfl_xor_sync(FULL, k, 2));
+        k = max(k, __shfl_xor_sync(FULL, k, 4));
+        if ((r & 7) == 0 && r < R) qmax[r >> 3] = (int)k;
+        m = max(m, k);
+      }
+    } else {
+      for (int r = tid; r < R; r += MQ_THREADS) m = max(m, (unsigned)max(klen[r], 0));
+    }
+    m = __reduce_max_sync(FULL, m);
+    if (l == 0) atomicMax(&kmax_all, m);
+  }
+  __syncthreads();
+  const unsigned kcap = min(kmax_all, (unsigned)stride);
+  const int nch = (int)(((kcap + MQ_KEYS - 1) / MQ_KEYS + MQ_CHUNK - 1) / MQ_CHUNK);
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer: bulk tensor copies
     uint32_t kit = 0, qit = 0, k_issued = 0;
     int q_issued = 0;
     bool ok = true;
-    for (long long i = blockIdx.x; ok && i < items; i += gridDim.x) {
-      const int qb = (int)(i / nch), c = (int)(i % nch);
-      if (!mq_item_has_tiles(row_seq, klen, R, qb, c)) continue;
+    for (MqItems it(nqb, nch); ok && it.valid(); it.next()) {
+      const int qb = it.qb, c = it.c;
+      if (!mq_item_has_tiles(qmax, klen, R, nqb, qb, c)) continue;
       const int qs = qit & 1;
       if (l == 0) {
         ok = mq_wait(smem_u32(&q_empty[qs]), ((qit >> 1) & 1) ^ 1, abort);
@@ -280,9 +324,9 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
     if (l == 0) {
       uint32_t kit = 0, qit = 0;
       bool ok = true, issued = false;
-      for (long long i = blockIdx.x; ok && i < items; i += gridDim.x) {
-        const int qb = (int)(i / nch), c = (int)(i % nch);
-        if (!mq_item_has_tiles(row_seq, klen, R, qb, c)) continue;
+      for (MqItems it(nqb, nch); ok && it.valid(); it.next()) {
+        const int qb = it.qb, c = it.c;
+        if (!mq_item_has_tiles(qmax, klen, R, nqb, qb, c)) continue;
         const int qs = qit & 1;
         if (!(ok = mq_wait(smem_u32(&q_full[qs]), (qit >> 1) & 1, abort))) break;
         const uint64_t bdesc = sw128_desc(qbuf + qs * MQ_QBYTES);
@@ -318,9 +362,9 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
     float* wsm = reinterpret_cast<float*>(sgen + (wbuf - sbase)) + (warp - 2) * 2 * IH;
     uint32_t kit = 0;
     bool ok = true;
-    for (long long i = blockIdx.x; ok && i < items; i += gridDim.x) {
-      const int qb = (int)(i / nch), c = (int)(i % nch);
-      if (!mq_item_has_tiles(row_seq, klen, R, qb, c)) continue;
+    for (MqItems it(nqb, nch); ok && it.valid(); it.next()) {
+      const int qb = it.qb, c = it.c;
+      if (!mq_item_has_tiles(qmax, klen, R, nqb, qb, c)) continue;
       const int ra = qb * MQ_ROWS + 2 * cq;  // this warp's rows ra, ra + 1
       // their head weights (zero past R), interleaved by head into the warp's shared-memory slice:
       // wsm[2 h + j] = w[ra + j][h], so one packed FMA takes head h of both rows
@@ -360,8 +404,10 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
             }
             const float2 sum = make_float2(__fadd_rn(acc0.x, acc1.x), __fadd_rn(acc0.y, acc1.y));
             if (p < stride) {
-              if (live0 && p < kl0) logits[(size_t)ra * stride + p] = __fmul_rn(sum.x, scale);
-              if (live1 && p < kl1) logits[(size_t)(ra + 1) * stride + p] = __fmul_rn(sum.y, scale);
+              // streaming stores: the logits pass through L2 without evicting the keys the other row
+              // blocks of the sequence still read
+              if (live0 && p < kl0) __stcs(logits + (size_t)ra * stride + p, __fmul_rn(sum.x, scale));
+              if (live1 && p < kl1) __stcs(logits + (size_t)(ra + 1) * stride + p, __fmul_rn(sum.y, scale));
             }
           }
           tc_fence_before();
