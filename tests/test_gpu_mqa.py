@@ -85,6 +85,61 @@ def test_mqa_logits_cfg0(cuda):
     _check(got, *case, "cfg0")
 
 
+def test_mqa_logits_stride_below_klen_and_sub_chunks(cuda):
+    """A stride below some rows' klen keeps every store inside the row (positions >= stride are not
+    written), and the rows scored in sub-chunks (the manifest's --sub) match one launch."""
+    import glmkv
+
+    case = _case([300, 0, 900], [40, 25, 19], seed=83)
+    call, pool, iq, w, row_seq, klen = case
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    R, stride = len(row_seq), 640  # rows of the third sequence reach klen 919
+    got = _run(cuda, *case, stride)
+    from oracle import mqa
+    want = mqa.mqa_logits_paged(iq, pool, call.block_table, call.max_pages, row_seq, klen, w)
+    for r, (lg, mg) in enumerate(want):
+        k = min(int(klen[r]), stride)
+        err = np.abs(got[r, :k].astype(np.float64) - lg[:k]) / np.maximum(mg[:k], 1e-30)
+        assert err.max() <= TOL, r
+        assert np.all(np.isnan(got[r, k:])), r
+    # the same rows in sub-chunks of 24 rows (block edges inside sequences), row pointers offset
+    sub = torch.full((R * stride,), float("nan"), dtype=torch.float32, device=cuda)
+    iq_d, w_d, rs_d, kl_d, bt_d, pool_d = t(iq), t(w), t(row_seq), t(klen), t(call.block_table), t(pool)
+    for j in range(0, R, 24):
+        n = min(24, R - j)
+        glmkv.mqa_logits_paged(iq_d[j * 4096:], pool_d, call.n_pages, bt_d, call.max_pages, rs_d[j:], kl_d[j:],
+                               w_d[j:], sub[j * stride:], stride, n)
+    torch.cuda.synchronize()
+    assert np.array_equal(sub.cpu().numpy().reshape(R, stride), got, equal_nan=True)
+
+
+def test_mqa_logits_bad_page_is_flagged(cuda):
+    """A block-table entry outside the pool is skipped (never read) and flagged; other sequences'
+    logits are unaffected."""
+    import glmkv
+
+    case = _case([200, 130], [30, 20], seed=84)
+    call, pool, iq, w, row_seq, klen = case
+    bt = call.block_table.copy()
+    bt[1, 1] = call.n_pages + 5  # sequence 1, positions 64 .. 127
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    R, stride = len(row_seq), 256
+    logits = torch.full((R * stride,), float("nan"), dtype=torch.float32, device=cuda)
+    glmkv.fault_flags()
+    glmkv.mqa_logits_paged(t(iq), t(pool), call.n_pages, t(bt), call.max_pages, t(row_seq), t(klen), t(w), logits,
+                           stride, R)
+    torch.cuda.synchronize()
+    assert glmkv.fault_flags() & 2
+    got = logits.cpu().numpy().reshape(R, stride)
+    from oracle import mqa
+    want = mqa.mqa_logits_paged(iq, pool, call.block_table, call.max_pages, row_seq, klen, w)
+    for r in range(R):
+        if row_seq[r] == 0:  # sequence 0 reads only its own pages
+            lg, mg = want[r]
+            err = np.abs(got[r, :klen[r]] - lg) / np.maximum(mg, 1e-30)
+            assert err.max() <= TOL, r
+
+
 def test_mqa_logits_rejects_bad_arguments():
     import glmkv
     from glmkv import _lib
