@@ -144,6 +144,15 @@ struct MqItems {
     if (qb >= nqb) qb -= nqb, ++c;
   }
 };
+// relu(x) * 2^-25 on the FMA pipe: saturate(x * 2^-25 + 0), which clamps to [0, 1]. A dot product of
+// 128 e4m3 pairs is below 128 * 448^2 < 2^25 in magnitude, so this is relu(x) scaled by an exact
+// power of two (the smallest nonzero |x|, 2^-18, stays a normal number), and with the head weights
+// scaled by 2^25 each product w * relu(x) rounds exactly as before. A NaN gives 0, as fmaxf(NaN, 0).
+__device__ __forceinline__ float relu_s(float x) {
+  float d;
+  asm("fma.rn.sat.f32 %0, %1, 0f33000000, 0f00000000;" : "=f"(d) : "f"(x));
+  return d;
+}
 struct MqSegment {
   int sb, se, seq, kmax, kb0, kb1;  // rows [sb, se), key tiles [kb0, kb1)
 };
@@ -373,8 +382,8 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
         const int j = l >> 4, h2 = 2 * (l & 15);
         const int r = ra + j;
         const float2 v = r < R ? __ldg(reinterpret_cast<const float2*>(w + (size_t)r * IH + h2)) : make_float2(0.f, 0.f);
-        wsm[2 * h2 + j] = v.x;
-        wsm[2 * h2 + 2 + j] = v.y;
+        wsm[2 * h2 + j] = v.x * 33554432.f;  // w * 2^25 (exact): relu(x) * w = relu_s(x) * (w * 2^25)
+        wsm[2 * h2 + 2 + j] = v.y * 33554432.f;
       }
       __syncwarp();
       const int kl0 = ra < R ? klen[ra] : 0, kl1 = ra + 1 < R ? klen[ra + 1] : 0;
@@ -399,8 +408,8 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
 #pragma unroll
             for (int h = 0; h < IH; h += 2) {
               const float4 ww = *reinterpret_cast<const float4*>(wsm + 2 * h);  // w[ra][h], w[ra+1][h], .. h + 1
-              acc0 = fma2(make_float2(ww.x, ww.y), make_float2(fmaxf(v[0][h], 0.f), fmaxf(v[1][h], 0.f)), acc0);
-              acc1 = fma2(make_float2(ww.z, ww.w), make_float2(fmaxf(v[0][h + 1], 0.f), fmaxf(v[1][h + 1], 0.f)), acc1);
+              acc0 = fma2(make_float2(ww.x, ww.y), make_float2(relu_s(v[0][h]), relu_s(v[1][h])), acc0);
+              acc1 = fma2(make_float2(ww.z, ww.w), make_float2(relu_s(v[0][h + 1]), relu_s(v[1][h + 1])), acc1);
             }
             const float2 sum = make_float2(__fadd_rn(acc0.x, acc1.x), __fadd_rn(acc0.y, acc1.y));
             if (p < stride) {
