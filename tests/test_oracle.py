@@ -278,3 +278,40 @@ def test_oracle_add_rms_quant_matches_reference(name):
         e = ss.reshape(12, T, 4).transpose(1, 0, 2).reshape(T, 48).astype(np.int32)
         return cpu.f32_from_e4m3(qq).reshape(T, 48, 128) * np.ldexp(1.0, e - 127)[:, :, None]
     assert_values_close(vals(q, sf), vals(ref["q"], ref["sf"]), E4M3_REL, f"{name}: q")
+
+
+def test_mqa_oracle_against_a_direct_loop():
+    """oracle/mqa.py (the restated fp8 MQA logits, read from the cache pages) against a plain loop over
+    rows, heads and keys on a small paged call, and its e4m3 table against ml_dtypes."""
+    import ml_dtypes
+
+    from glmkv import workload as W
+    from oracle import mqa
+
+    codes = np.arange(256, dtype=np.uint8)
+    ref = codes.view(ml_dtypes.float8_e4m3fn).astype(np.float64)
+    same = (mqa.E4M3 == ref) | (np.isnan(mqa.E4M3) & np.isnan(ref))
+    assert same.all()
+
+    rng = np.random.default_rng(7)
+    call = W.make_call([70, 0, 5], [3, 4, 2], rng, spare_pages=1)
+    pool = np.empty((call.n_pages, 64 * 132), np.uint8)
+    c = rng.integers(0, 256, size=(call.n_pages, 8192), dtype=np.uint8)
+    pool[:, :8192] = np.where((c & 0x7F) == 0x7F, c - 1, c)
+    pool[:, 8192:] = np.exp2(rng.integers(-6, 3, size=(call.n_pages, 64))).astype(np.float32).view(np.uint8)
+    R = call.T
+    iq = rng.integers(0, 126, size=R * 32 * 128, dtype=np.uint8)
+    w = rng.standard_normal((R, 32)).astype(np.float32)
+    row_seq = np.repeat(np.arange(call.nseq, dtype=np.int32), call.fresh)
+    klen = (W.positions(call) + 1).astype(np.int32)
+    got = mqa.mqa_logits_paged(iq, pool, call.block_table, call.max_pages, row_seq, klen, w)
+    q = mqa.E4M3[iq.reshape(R, 32, 128)]
+    for r in range(R):
+        s = row_seq[r]
+        for p in range(klen[r]):
+            page, row = call.block_table[s, p // 64], p % 64
+            k = mqa.E4M3[pool[page, row * 128:(row + 1) * 128]]
+            sc = float(pool[page, 8192 + 4 * row:8196 + 4 * row].view(np.float32)[0])
+            want = sum(float(w[r, h]) * max(float(q[r, h] @ k) * sc, 0.0) for h in range(32))
+            lg, mg = got[r]
+            assert abs(lg[p] - want) <= 1e-12 * max(mg[p], 1e-30), (r, p)
