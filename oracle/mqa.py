@@ -1,4 +1,5 @@
-"""The indexer's fp8 MQA logits, restated in NumPy. TEST INFRASTRUCTURE ONLY.
+"""The indexer's fp8 MQA logits, restated in NumPy. TEST INFRASTRUCTURE ONLY. Parity unpinned: the
+reference's own kernel for this (DeepGEMM) is absent, so no reference output exists to pin it to.
 
 kern-glm53 scores each fresh row against every key of its sequence with DeepGEMM's sm100 fp8 MQA
 logits (scripts/glm_ops.py:104-134: ``MQA_ENTRY``, launched on the gathered ``kg`` / ``ksf`` stream
