@@ -833,7 +833,7 @@ constexpr int HID = 6144;                 // the residual stream's width
 constexpr int ARQ_THREADS = 256;          // the reference's thread (w, l) layout, kept for its sums
 constexpr int ARQ_ROW = HID * 2;          // 12288 B
 constexpr int ARQ_STAGES = 2;
-constexpr int ARQ_SMEM = ARQ_STAGES * 2 * ARQ_ROW;  // res and a rows, two stages: 49152 B
+constexpr int ARQ_SMEM = ARQ_STAGES * 2 * ARQ_ROW;  // res and a rows of each stage: 49,152 B for two
 constexpr int QT_THREADS = 256;
 
 // max(|.|) of the eight bf16 values in a uint4, as f32
@@ -882,15 +882,24 @@ extern "C" __global__ void __launch_bounds__(glmkv::ARQ_THREADS, 3)
   uint2 gw[6];  // gamma of this thread's columns
 #pragma unroll
   for (int i = 0; i < 6; ++i) gw[i] = __ldg(reinterpret_cast<const uint2*>(gamma + (w * 6 + i) * 128 + l * 4));
-  if (tid == 0) issue(0, r);
+  // rows r, r + G, ..., the next ARQ_STAGES - 1 of them always on their way (G = the grid)
+  const long long G = gridDim.x;
+  if (tid == 0)
+    for (int j = 0; j < ARQ_STAGES - 1; ++j)
+      if (r + j * G < T) issue(j, (int)(r + j * G));
   for (int k = 0; r < T; ++k, r += gridDim.x) {
-    const int st = k & 1, rn = r + gridDim.x;
-    if (rn < T && tid == 0) issue(st ^ 1, rn);  // that stage's row is done: block_sum synced past it
-    const bool ok = mbar_wait_bounded(smem_u32(&full[st]), (uint32_t)((k >> 1) & 1), WAIT_LIMIT_NS);
+    const int st = k % ARQ_STAGES;
+    const long long rn = r + (ARQ_STAGES - 1) * G;
+    // that stage held row k - 1, whose reads all came before the block_sum barriers of its iteration
+    if (rn < T && tid == 0) issue((k + ARQ_STAGES - 1) % ARQ_STAGES, (int)rn);
+    const bool ok = mbar_wait_bounded(smem_u32(&full[st]), (uint32_t)((k / ARQ_STAGES) & 1), WAIT_LIMIT_NS);
     if (__syncthreads_or(!ok)) {
-      if (tid == 0) {
+      if (tid == 0) {  // flag it, and wait (bounded) for the copies in flight
         atomicOr(&g_fault, FAULT_WAIT_TIMEOUT);
-        if (rn < T) mbar_wait_bounded(smem_u32(&full[st ^ 1]), (uint32_t)(((k + 1) >> 1) & 1), WAIT_LIMIT_NS);
+        for (int j = 1; j < ARQ_STAGES; ++j)
+          if (r + j * G < T)
+            mbar_wait_bounded(smem_u32(&full[(k + j) % ARQ_STAGES]), (uint32_t)(((k + j) / ARQ_STAGES) & 1),
+                              WAIT_LIMIT_NS);
       }
       return;
     }
