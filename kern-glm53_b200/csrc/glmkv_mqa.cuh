@@ -10,21 +10,25 @@
 // logits at [r][0, ke - ks)); the scale is non-negative, so relu(dot * s) = relu(dot) * s.
 //
 // One CTA per SM, warp-specialised, on Blackwell's tensor cores:
-//  - warp 0 (one lane): bulk tensor copies (TMA, 128-byte swizzle) of a block of 8 query rows
+//  - warp 0: walks the work items (the warp reads a block's rows and block-table entries together)
+//    and one lane issues bulk tensor copies (TMA, 128-byte swizzle) of a block of 8 query rows
 //    (256 (row, head) rows of 128 bytes) and of key tiles (two 64-key pages, straight from the cache)
-//    into a ring of shared-memory stages;
-//  - warp 1: allocates 512 TMEM columns; one lane issues tcgen05.mma kind::f8f6f4 (e4m3 x e4m3 -> f32),
-//    M = 128 keys x N = 256 (row, head) x K = 128 (four K = 32 steps) into one of two TMEM
-//    accumulators, and commits each stage and accumulator back to its barrier;
-//  - warps 2..9: the epilogue. Warp w reads TMEM lanes 32 (w % 4) .. + 31 (one key a thread) and half
-//    of the columns (four query rows), then relu, the head-weighted sum and the key's scale, and
-//    stores the logit (32 consecutive keys a warp: 128-byte coalesced rows).
+//    into a ring of shared-memory stages, each with a descriptor word for the MMA issuer;
+//  - warp 1: allocates 512 TMEM columns; one lane, driven by the stage descriptors, issues
+//    tcgen05.mma kind::f8f6f4 (e4m3 x e4m3 -> f32), M = 128 keys x N = 256 (row, head) x K = 128
+//    (four K = 32 steps) into one of two TMEM accumulators, and commits each stage and accumulator
+//    back to its barrier;
+//  - warps 2..17: the epilogue. Warp w reads TMEM lanes 32 (w % 4) .. + 31 (one key a thread) and
+//    the 64 columns of two query rows, then relu, the head-weighted sum and the key's scale, and
+//    stores the logits (32 consecutive keys a warp: 128-byte coalesced rows).
 // A block of rows that spans two sequences is worked as two segments over the same query stage.
 // Every wait is bounded; a wait that gives up sets the fault word, stops every role, waits for the
 // copies and MMAs in flight and frees TMEM before returning.
 #pragma once
 
 #include <cuda.h>
+
+#include <climits>
 
 #include "glmkv_kernels.cuh"
 
@@ -43,6 +47,9 @@ constexpr int MQ_THREADS = 32 * (2 + MQ_EPI_WARPS);
 constexpr int MQ_TMEM_COLS = 2 * MQ_N;           // two f32 accumulators of 256 columns
 constexpr int MQ_WBYTES = MQ_EPI_WARPS * 2 * IH * 4;  // each epilogue warp's two rows of head weights
 constexpr int MQ_QTAB = 4096;                    // blocks whose largest klen is kept in shared memory
+// A key stage's descriptor word, written by the producer before the stage's copies: the first tile
+// of a work item (the MMA issuer then waits for the item's query stage), or the end of the launch.
+constexpr uint32_t MQ_D_FIRST = 1u, MQ_D_END = 2u;
 constexpr int MQ_SMEM = 1024 + 2 * MQ_QBYTES + MQ_KSTAGES * (MQ_KBYTES + MQ_SCBYTES) + MQ_WBYTES;  // + 1 KB: align
 // instruction descriptor, kind::f8f6f4: D f32 (bits 4-5 = 1), A and B e4m3 (0), both K-major (0),
 // N >> 3 at bits 17-22, M >> 4 at bits 24-28
@@ -156,34 +163,54 @@ __device__ __forceinline__ float relu_s(float x) {
 struct MqSegment {
   int sb, se, seq, kmax, kb0, kb1;  // rows [sb, se), key tiles [kb0, kb1)
 };
-// f(segment) for each segment of block qb with key tiles in chunk c; false as soon as f returns false.
+// The rows of block qb as a warp holds them: lane j < 8 has row qb * 8 + j's sequence and klen
+// (-1 and 0 past R): two loads a lane, one round trip for the block.
+struct MqRows {
+  int seq, kl;
+};
+__device__ __forceinline__ MqRows mq_load_rows(const int* __restrict__ row_seq, const int* __restrict__ klen, int R,
+                                               int qb) {
+  const int l = threadIdx.x & 31, r = qb * MQ_ROWS + l;
+  MqRows v{-1, 0};
+  if (l < MQ_ROWS && r < R) v = MqRows{__ldg(row_seq + r), __ldg(klen + r)};
+  return v;
+}
+// f(segment) for each segment (a run of rows of one sequence) of block qb with key tiles in chunk c;
+// false as soon as f returns false. Warp-collective: every lane calls it with the block's rows.
 template <class F>
-__device__ __forceinline__ bool mq_segments(const int* __restrict__ row_seq, const int* __restrict__ klen, int R, int qb,
-                                            int c, F&& f) {
-  const int r0 = qb * MQ_ROWS, re = min(r0 + MQ_ROWS, R);
-  for (int sb = r0; sb < re;) {
-    const int s = row_seq[sb];
-    int se = sb + 1, kmax = klen[sb];
-    while (se < re && row_seq[se] == s) kmax = max(kmax, klen[se++]);
+__device__ __forceinline__ bool mq_segments(const MqRows& v, int R, int qb, int c, F&& f) {
+  const int l = threadIdx.x & 31, r0 = qb * MQ_ROWS, n = min(MQ_ROWS, R - r0);
+  const int prev = __shfl_up_sync(FULL, v.seq, 1);
+  unsigned starts = __ballot_sync(FULL, l < n && (l == 0 || v.seq != prev));  // the first row of each segment
+  while (starts) {
+    const int sb = __ffs(starts) - 1;
+    starts &= starts - 1;
+    const int se = starts ? __ffs(starts) - 1 : n;
+    const int kmax = __reduce_max_sync(FULL, l >= sb && l < se ? v.kl : INT_MIN);
+    const int s = __shfl_sync(FULL, v.seq, sb);
     const int nkb = (kmax + MQ_KEYS - 1) / MQ_KEYS;
     const int kb0 = c * MQ_CHUNK, kb1 = min(kb0 + MQ_CHUNK, nkb);
-    if (kb0 < kb1 && !f(MqSegment{sb, se, s, kmax, kb0, kb1})) return false;
-    sb = se;
+    if (kb0 < kb1 && !f(MqSegment{r0 + sb, r0 + se, s, kmax, kb0, kb1})) return false;
   }
   return true;
 }
 // Whether item (qb, c) has any tile: a segment has tiles in chunk c when its largest klen passes
 // c * 2048, so the item has some when the block's largest klen does. `qmax` holds every block's
-// largest klen when the launch has at most MQ_QTAB blocks; otherwise the rows are read here.
-__device__ __forceinline__ int mq_block_kmax(const int* __restrict__ klen, int R, int qb) {
-  int m = 0;
-  for (int r = qb * MQ_ROWS; r < min(qb * MQ_ROWS + MQ_ROWS, R); ++r) m = max(m, klen[r]);
-  return m;
-}
+// largest klen when the launch has at most MQ_QTAB blocks; otherwise the warp reads the rows here.
 __device__ __forceinline__ bool mq_item_has_tiles(const int* qmax, const int* __restrict__ klen, int R, int nqb, int qb,
                                                   int c) {
-  const int m = nqb <= MQ_QTAB ? qmax[qb] : mq_block_kmax(klen, R, qb);
+  int m;
+  if (nqb <= MQ_QTAB) {
+    m = qmax[qb];
+  } else {
+    const int l = threadIdx.x & 31, r = qb * MQ_ROWS + l;
+    m = __reduce_max_sync(FULL, l < MQ_ROWS && r < R ? max(__ldg(klen + r), 0) : 0);
+  }
   return m > c * MQ_CHUNK * MQ_KEYS;
+}
+// Moves `it` to the first item at or after it with key tiles. Warp-collective.
+__device__ __forceinline__ void mq_skip_empty(MqItems& it, const int* qmax, const int* __restrict__ klen, int R) {
+  while (it.valid() && !mq_item_has_tiles(qmax, klen, R, it.nqb, it.qb, it.c)) it.next();
 }
 
 __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const u8* __restrict__ idx,
@@ -195,6 +222,7 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
       acc_full[2], acc_empty[2], mma_done;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
+  __shared__ uint32_t kdesc[MQ_KSTAGES];  // each key stage's descriptor word (MQ_D_*)
   __shared__ unsigned kmax_all;  // the largest klen of the launch's rows
   __shared__ int qmax[MQ_QTAB];  // each block's largest klen (launches of at most MQ_QTAB blocks)
   const int tid = threadIdx.x, warp = tid >> 5, l = tid & 31;
@@ -264,9 +292,11 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
     uint32_t kit = 0, qit = 0, k_issued = 0;
     int q_issued = 0;
     bool ok = true;
-    for (MqItems it(nqb, nch); ok && it.valid(); it.next()) {
+    MqItems it(nqb, nch);
+    mq_skip_empty(it, qmax, klen, R);
+    while (ok && it.valid()) {
       const int qb = it.qb, c = it.c;
-      if (!mq_item_has_tiles(qmax, klen, R, nqb, qb, c)) continue;
+      const MqRows rows = mq_load_rows(row_seq, klen, R, qb);
       const int qs = qit & 1;
       if (l == 0) {
         ok = mq_wait(smem_u32(&q_empty[qs]), ((qit >> 1) & 1) ^ 1, abort);
@@ -279,7 +309,8 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
       if (!ok) break;
       q_issued |= 1 << qs;
       ++qit;
-      ok = mq_segments(row_seq, klen, R, qb, c, [&](const MqSegment& g) {
+      uint32_t first = MQ_D_FIRST;
+      ok = mq_segments(rows, R, qb, c, [&](const MqSegment& g) {
         // lane j holds the page of position block 2 kb0 + j (the item's up to 32 pages)
         const int pj = 2 * g.kb0 + l;
         int pg = -1;
@@ -295,6 +326,7 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
           if (l == 0) {
             okk = mq_wait(smem_u32(&k_empty[st]), ((kit / MQ_KSTAGES) & 1) ^ 1, abort);
             if (okk) {
+              kdesc[st] = first;  // published by the arrive below
               const uint32_t bytes = (p0 >= 0 ? MQ_KBYTES / 2 + MQ_SCBYTES / 2 : 0) +
                                      (p1 >= 0 ? MQ_KBYTES / 2 + MQ_SCBYTES / 2 : 0);
               mbar_arrive_expect_tx(smem_u32(&k_full[st]), bytes);
@@ -310,10 +342,23 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
           }
           if (!__shfl_sync(FULL, okk, 0)) return false;
           k_issued |= 1u << st;
+          first = 0;
           ++kit;
         }
         return true;
       });
+      it.next();
+      mq_skip_empty(it, qmax, klen, R);
+    }
+    if (ok && l == 0) {  // the end marker: a stage with no copies, completed by a plain arrive
+      const int st = kit % MQ_KSTAGES;
+      ok = mq_wait(smem_u32(&k_empty[st]), ((kit / MQ_KSTAGES) & 1) ^ 1, abort);
+      if (ok) {
+        kdesc[st] = MQ_D_END;
+        mbar_arrive(smem_u32(&k_full[st]));
+        k_issued |= 1u << st;
+        ++kit;
+      }
     }
     if (!ok && l == 0) give_up();
     if (l == 0) {  // wait (bounded) for every copy still in flight: the last phase of each stage used
@@ -330,34 +375,34 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issue (one lane)
+    // Driven by the stage descriptors: no walk of the items here, so the lane does little besides
+    // waiting and issuing. A work item's query stage is released when the next item starts.
     if (l == 0) {
-      uint32_t kit = 0, qit = 0;
+      uint32_t st = 0, kph = 0, tile = 0, qit = 0;
       bool ok = true, issued = false;
-      for (MqItems it(nqb, nch); ok && it.valid(); it.next()) {
-        const int qb = it.qb, c = it.c;
-        if (!mq_item_has_tiles(qmax, klen, R, nqb, qb, c)) continue;
-        const int qs = qit & 1;
-        if (!(ok = mq_wait(smem_u32(&q_full[qs]), (qit >> 1) & 1, abort))) break;
-        const uint64_t bdesc = sw128_desc(qbuf + qs * MQ_QBYTES);
-        ok = mq_segments(row_seq, klen, R, qb, c, [&](const MqSegment& g) {
-          for (int kb = g.kb0; kb < g.kb1; ++kb) {
-            const int st = kit % MQ_KSTAGES, a = kit & 1;
-            if (!mq_wait(smem_u32(&k_full[st]), (kit / MQ_KSTAGES) & 1, abort)) return false;
-            if (!mq_wait(smem_u32(&acc_empty[a]), ((kit >> 1) & 1) ^ 1, abort)) return false;
-            tc_fence_after();
-            const uint64_t adesc = sw128_desc(kbuf + st * MQ_KBYTES);
+      uint64_t bdesc = 0;
+      for (;;) {
+        if (!(ok = mq_wait(smem_u32(&k_full[st]), kph, abort))) break;
+        const uint32_t d = kdesc[st];
+        if (d & MQ_D_END) break;
+        if (d & MQ_D_FIRST) {
+          if (qit > 0) tc_commit(smem_u32(&q_empty[(qit - 1) & 1]));
+          if (!(ok = mq_wait(smem_u32(&q_full[qit & 1]), (qit >> 1) & 1, abort))) break;
+          bdesc = sw128_desc(qbuf + (qit & 1) * MQ_QBYTES);
+          ++qit;
+        }
+        const uint32_t a = tile & 1;
+        if (!(ok = mq_wait(smem_u32(&acc_empty[a]), ((tile >> 1) & 1) ^ 1, abort))) break;
+        tc_fence_after();
+        const uint64_t adesc = sw128_desc(kbuf + st * MQ_KBYTES);
 #pragma unroll
-            for (int kk = 0; kk < ID / 32; ++kk)
-              tc_mma(tmem + a * MQ_N, adesc + 2 * kk, bdesc + 2 * kk, MQ_IDESC, kk > 0);
-            issued = true;
-            tc_commit(smem_u32(&k_empty[st]));
-            tc_commit(smem_u32(&acc_full[a]));
-            ++kit;
-          }
-          return true;
-        });
-        if (ok) tc_commit(smem_u32(&q_empty[qs]));
-        ++qit;
+        for (int kk = 0; kk < ID / 32; ++kk)
+          tc_mma(tmem + a * MQ_N, adesc + 2 * kk, bdesc + 2 * kk, MQ_IDESC, kk > 0);
+        issued = true;
+        tc_commit(smem_u32(&k_empty[st]));
+        tc_commit(smem_u32(&acc_full[a]));
+        ++tile;
+        if (++st == MQ_KSTAGES) st = 0, kph ^= 1;
       }
       if (!ok) give_up();
       if (issued) {  // every MMA has completed before TMEM is freed
@@ -371,23 +416,29 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
     float* wsm = reinterpret_cast<float*>(sgen + (wbuf - sbase)) + (warp - 2) * 2 * IH;
     uint32_t kit = 0;
     bool ok = true;
-    for (MqItems it(nqb, nch); ok && it.valid(); it.next()) {
+    // this lane's share of a block's head weights: row 2 cq + (l >> 4), heads 2 (l & 15) and + 1
+    auto load_w = [&](int qb) {
+      const int r = qb * MQ_ROWS + 2 * cq + (l >> 4);
+      return r < R ? __ldg(reinterpret_cast<const float2*>(w + (size_t)r * IH + 2 * (l & 15))) : make_float2(0.f, 0.f);
+    };
+    MqItems it(nqb, nch);
+    mq_skip_empty(it, qmax, klen, R);
+    while (ok && it.valid()) {
       const int qb = it.qb, c = it.c;
-      if (!mq_item_has_tiles(qmax, klen, R, nqb, qb, c)) continue;
+      const MqRows rows = mq_load_rows(row_seq, klen, R, qb);
+      const float2 wv = load_w(qb);
       const int ra = qb * MQ_ROWS + 2 * cq;  // this warp's rows ra, ra + 1
       // their head weights (zero past R), interleaved by head into the warp's shared-memory slice:
       // wsm[2 h + j] = w[ra + j][h], so one packed FMA takes head h of both rows
       __syncwarp();
       {
         const int j = l >> 4, h2 = 2 * (l & 15);
-        const int r = ra + j;
-        const float2 v = r < R ? __ldg(reinterpret_cast<const float2*>(w + (size_t)r * IH + h2)) : make_float2(0.f, 0.f);
-        wsm[2 * h2 + j] = v.x * 33554432.f;  // w * 2^25 (exact): relu(x) * w = relu_s(x) * (w * 2^25)
-        wsm[2 * h2 + 2 + j] = v.y * 33554432.f;
+        wsm[2 * h2 + j] = wv.x * 33554432.f;  // w * 2^25 (exact): relu(x) * w = relu_s(x) * (w * 2^25)
+        wsm[2 * h2 + 2 + j] = wv.y * 33554432.f;
       }
       __syncwarp();
-      const int kl0 = ra < R ? klen[ra] : 0, kl1 = ra + 1 < R ? klen[ra + 1] : 0;
-      ok = mq_segments(row_seq, klen, R, qb, c, [&](const MqSegment& g) {
+      const int kl0 = __shfl_sync(FULL, rows.kl, 2 * cq), kl1 = __shfl_sync(FULL, rows.kl, 2 * cq + 1);
+      ok = mq_segments(rows, R, qb, c, [&](const MqSegment& g) {
         const bool live0 = ra >= g.sb && ra < g.se, live1 = ra + 1 >= g.sb && ra + 1 < g.se;
         for (int kb = g.kb0; kb < g.kb1; ++kb) {
           const int st = kit % MQ_KSTAGES, a = kit & 1;
@@ -426,6 +477,8 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
         }
         return true;
       });
+      it.next();
+      mq_skip_empty(it, qmax, klen, R);
     }
     if (!ok && l == 0) give_up();
   }
