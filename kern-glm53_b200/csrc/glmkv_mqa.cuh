@@ -239,7 +239,7 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
     }
     for (int i = 0; i < MQ_KSTAGES; ++i) {
       mbar_init(smem_u32(&k_full[i]), 1);
-      mbar_init(smem_u32(&k_empty[i]), 1 + MQ_EPI_WARPS);  // the MMAs, and every epilogue warp's scale read
+      mbar_init(smem_u32(&k_empty[i]), 1 + MQ_EPI_WARPS);  // the MMAs, and every epilogue warp at the tile's end
     }
     mbar_init(smem_u32(&mma_done), 1);
     mbar_init_fence();
@@ -414,7 +414,7 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
     // ---------------------------------------------------------------- epilogue: TMEM -> logits
     const int qd = warp & 3, cq = (warp - 2) >> 2;  // TMEM lane quarter; query rows 2 cq, 2 cq + 1 of a block
     float* wsm = reinterpret_cast<float*>(sgen + (wbuf - sbase)) + (warp - 2) * 2 * IH;
-    uint32_t kit = 0;
+    uint32_t est = 0, ea = 0, eph = 0;  // key stage, accumulator and its phase of the next tile
     bool ok = true;
     // this lane's share of a block's head weights: row 2 cq + (l >> 4), heads 2 (l & 15) and + 1
     auto load_w = [&](int qb) {
@@ -438,18 +438,20 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
       }
       __syncwarp();
       const int kl0 = __shfl_sync(FULL, rows.kl, 2 * cq), kl1 = __shfl_sync(FULL, rows.kl, 2 * cq + 1);
+      float* const out0 = logits + (size_t)ra * stride;
       ok = mq_segments(rows, R, qb, c, [&](const MqSegment& g) {
-        const bool live0 = ra >= g.sb && ra < g.se, live1 = ra + 1 >= g.sb && ra + 1 < g.se;
+        // the positions each row stores: below its klen and the stride, in its own segment only
+        const int lim0 = ra >= g.sb && ra < g.se ? min(kl0, stride) : 0;
+        const int lim1 = ra + 1 >= g.sb && ra + 1 < g.se ? min(kl1, stride) : 0;
+        const int lim = max(lim0, lim1);
         for (int kb = g.kb0; kb < g.kb1; ++kb) {
-          const int st = kit % MQ_KSTAGES, a = kit & 1;
-          const bool okw = mq_wait(smem_u32(&acc_full[a]), (kit >> 1) & 1, abort);
+          const bool okw = mq_wait(smem_u32(&acc_full[ea]), eph, abort);
           if (__any_sync(FULL, !okw)) return false;  // the warp leaves together: tcgen05.ld is warp-collective
           tc_fence_after();
           const int p = kb * MQ_KEYS + 32 * qd + l;  // this thread's key position
-          const float scale = reinterpret_cast<const float*>(sgen + (scbuf - sbase) + st * MQ_SCBYTES)[32 * qd + l];
-          __syncwarp();
-          if (l == 0) mbar_arrive(smem_u32(&k_empty[st]));  // the stage's scales are read
-          if (live0 || live1) {
+          const int a = ea;
+          if (kb * MQ_KEYS + 32 * qd < lim) {  // some lane of the warp stores
+            const float scale = reinterpret_cast<const float*>(sgen + (scbuf - sbase) + est * MQ_SCBYTES)[32 * qd + l];
             float v[2][32];
             tc_ld32(tmem + a * MQ_N + ((uint32_t)(32 * qd) << 16) + 2 * cq * IH, v[0]);
             tc_ld32(tmem + a * MQ_N + ((uint32_t)(32 * qd) << 16) + (2 * cq + 1) * IH, v[1]);
@@ -463,17 +465,20 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
               acc1 = fma2(make_float2(ww.z, ww.w), make_float2(relu_s(v[0][h + 1]), relu_s(v[1][h + 1])), acc1);
             }
             const float2 sum = make_float2(__fadd_rn(acc0.x, acc1.x), __fadd_rn(acc0.y, acc1.y));
-            if (p < stride) {
-              // streaming stores: the logits pass through L2 without evicting the keys the other row
-              // blocks of the sequence still read
-              if (live0 && p < kl0) __stcs(logits + (size_t)ra * stride + p, __fmul_rn(sum.x, scale));
-              if (live1 && p < kl1) __stcs(logits + (size_t)(ra + 1) * stride + p, __fmul_rn(sum.y, scale));
-            }
+            // streaming stores: the logits pass through L2 without evicting the keys the other row
+            // blocks of the sequence still read
+            if (p < lim0) __stcs(out0 + p, __fmul_rn(sum.x, scale));
+            if (p < lim1) __stcs(out0 + stride + p, __fmul_rn(sum.y, scale));
           }
           tc_fence_before();
           __syncwarp();
-          if (l == 0) mbar_arrive(smem_u32(&acc_empty[a]));
-          ++kit;
+          if (l == 0) {  // the stage (its scales) and the accumulator are read
+            mbar_arrive(smem_u32(&k_empty[est]));
+            mbar_arrive(smem_u32(&acc_empty[ea]));
+          }
+          if (++est == MQ_KSTAGES) est = 0;
+          ea ^= 1;
+          eph ^= ea ^ 1;  // the accumulator phase flips once both have been used
         }
         return true;
       });
