@@ -150,3 +150,52 @@ def test_mqa_logits_rejects_bad_arguments():
     assert L.glmkv_mqa_logits_paged(A, A, 0, A, 1, A, A, A, A, 16, 8, None) == _lib.ERR_ARG
     assert L.glmkv_mqa_logits_paged(A + 8, A, 1, A, 1, A, A, A, A, 16, 8, None) == _lib.ERR_ALIGN
     assert L.glmkv_mqa_logits_paged(A, A, 1, A, 1, A, A, A, A, 16, 0, None) == _lib.OK
+
+
+def test_mqa_logits_full_size_cfg3(cuda):
+    """The bench's cfg3 call at full size (16,384 rows, up to 262,912 keys a row), in the manifest's
+    1,024-row sub-chunks: 16 rows spread over the call against the oracle, and the first 4,096 rows
+    bit-identical to one 4,096-row launch (the logits do not depend on how the rows are split)."""
+    import glmkv
+    from glmkv import workload as W
+    from oracle import mqa
+
+    c3 = W.config("cfg3", seed=0)
+    case = _case(c3.prefix, c3.fresh, seed=85)
+    call, pool, iq, w, row_seq, klen = case
+    R, stride, sub = len(row_seq), int(klen.max()), 1024
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    iq_d, w_d, rs_d, kl_d, bt_d, pool_d = t(iq), t(w), t(row_seq), t(klen), t(call.block_table), t(pool)
+
+    def launch(out, j, n):
+        glmkv.mqa_logits_paged(iq_d[j * 4096:], pool_d, call.n_pages, bt_d, call.max_pages, rs_d[j:], kl_d[j:],
+                               w_d[j:], out, stride, n)
+
+    sample = np.linspace(0, R - 1, 16).astype(int)
+    got = {}
+    first = torch.full((4096 * stride,), float("nan"), dtype=torch.float32, device=cuda)
+    buf = torch.empty((sub * stride,), dtype=torch.float32, device=cuda)
+    for j in range(0, R, sub):
+        buf.fill_(float("nan"))
+        launch(buf, j, sub)
+        torch.cuda.synchronize()
+        assert glmkv.fault_flags() == 0
+        if j < 4096:
+            first[j * stride:(j + sub) * stride].copy_(buf)
+        for r in sample[(sample >= j) & (sample < j + sub)]:
+            got[int(r)] = buf[(r - j) * stride:(r - j) * stride + int(klen[r])].cpu().numpy().astype(np.float64)
+    whole = torch.full((4096 * stride,), float("nan"), dtype=torch.float32, device=cuda)
+    launch(whole, 0, 4096)
+    torch.cuda.synchronize()
+    assert torch.equal(whole.view(torch.int32), first.view(torch.int32))
+    del whole, first, buf
+
+    rows = np.array(sorted(got))
+    iq_rows = iq.reshape(R, 32 * 128)[rows]
+    want = mqa.mqa_logits_paged(iq_rows, pool, call.block_table, call.max_pages, row_seq[rows], klen[rows], w[rows])
+    worst = 0.0
+    for r, (lg, mg) in zip(rows, want):
+        err = np.abs(got[r] - lg) / np.maximum(mg, 1e-30)
+        worst = max(worst, float(err.max()))
+        assert err.max() <= TOL, f"row {r} position {int(err.argmax())}"
+    print(f"cfg3: {len(rows)} rows up to {int(klen[rows].max())} keys, worst error {worst:.3g} of magnitude")
