@@ -2,9 +2,9 @@
 tcgen05.mma from shared memory in the kernel's own operand layout and instruction descriptor, with no
 copies and no epilogue, in e4m3 and in bf16.
 
-The e4m3 kind must run at about twice the bf16 rate per SM clock (the dense fp8 rate of the part): that checks
-that the MQA's descriptor selects the full-rate fp8 path. The printed rates are the ceiling the MQA's
-TFLOP/s is read against."""
+The e4m3 kind must run at about twice the bf16 rate per SM clock (the dense fp8 rate of the part):
+that checks that the MQA's descriptor selects the full-rate fp8 path. The printed rates are the
+ceiling the MQA's TFLOP/s is read against."""
 import os
 import pathlib
 import shutil
