@@ -1,6 +1,6 @@
 """ctypes binding of ``libglmkv.so`` (the C ABI in ``include/glmkv.h``).
 
-The library is built in-tree by ``kern-glm53_b200/build.py``; loading fails loudly when it is missing
+The library is built in-tree by ``kern-glm53_b200/glmkv/build.py``; loading fails loudly when it is missing
 (there is no other implementation to fall back to).
 """
 import ctypes
