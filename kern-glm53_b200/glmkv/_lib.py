@@ -1,7 +1,7 @@
 """ctypes binding of ``libglmkv.so`` (the C ABI in ``include/glmkv.h``).
 
-The library is built in-tree by ``kern-glm53_b200/glmkv/build.py``; loading fails loudly when it is missing
-(there is no other implementation to fall back to).
+The library is built in-tree by ``kern-glm53_b200/glmkv/build.py``; loading fails loudly when it is
+missing (there is no other implementation to fall back to).
 """
 import ctypes
 import pathlib
