@@ -133,12 +133,12 @@ __device__ __forceinline__ bool mq_wait(uint32_t bar, uint32_t parity, const vol
 }
 
 // The work of a launch is a grid of items (query block qb of 8 rows, key chunk c of 16 tiles = 2048
-// positions), item i = qb * nch + c going to CTA i % G. An item covers, in each segment of its block
-// (a run of rows of one sequence), the key tiles c * 16 .. c * 16 + 15 below the segment's largest
-// klen; an item with none is skipped by every role alike. Every role walks the items in this order.
-// The items of this CTA, blockIdx.x, + G, + 2 G, ..., numbered chunk-major (i = c * nqb + qb, so the
-// first chunk of every block comes before any second chunk), as (block qb, chunk c) without a
-// division a step: G = cg * nqb + qg. The walk ends at the first chunk no row of the launch reaches.
+// positions), numbered chunk-major: item i = c * nqb + qb, so the first chunk of every block comes
+// before any second chunk. Item i goes to CTA i % G. An item covers, in each segment of its block (a
+// run of rows of one sequence), the key tiles c * 16 .. c * 16 + 15 below the segment's largest klen;
+// an item with none is skipped by every role alike, and every role walks the items in the same order.
+// MqItems steps through this CTA's items, blockIdx.x, + G, + 2 G, ..., as (block qb, chunk c) without
+// a division a step: G = cg * nqb + qg. The walk ends at the first chunk no row of the launch reaches.
 struct MqItems {
   int qb, c, nqb, nch, qg, cg;
   __device__ __forceinline__ MqItems(int nqb_, int nch_)
