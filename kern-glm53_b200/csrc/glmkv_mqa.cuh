@@ -92,22 +92,28 @@ __device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint3
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
-// 32 f32 columns of this warp's 32 TMEM lanes (one lane a thread) at `taddr`, then wait for them.
-__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
+// 16 f32 columns of this warp's 32 TMEM lanes (one lane a thread) at `taddr`. The registers are valid
+// after tc_ld16_wait; every register of a load issued before that wait passes through it (or through
+// tc_ld16_after), so that no read of them moves above the wait.
+__device__ __forceinline__ void tc_ld16_issue(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
-
+__device__ __forceinline__ void tc_ld16_wait(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]),
+        "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+      :: "memory");
+}
+__device__ __forceinline__ void tc_ld16_after(uint32_t (&r)[16]) {
+  asm volatile(""
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]),
+        "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+      :: "memory");
+}
 // try_wait with a suspend-time hint: the warp sleeps until the phase completes (or `hint_ns` pass)
 // instead of spinning, so waiting warps leave the issue slots to the working ones.
 __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
@@ -437,6 +443,9 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
         wsm[2 * h2 + 2 + j] = wv.y * 33554432.f;
       }
       __syncwarp();
+      float4 wr[8];  // heads 0 .. 15 of both rows, held in registers for the item
+#pragma unroll
+      for (int i = 0; i < 8; ++i) wr[i] = *reinterpret_cast<const float4*>(wsm + 4 * i);
       const int kl0 = __shfl_sync(FULL, rows.kl, 2 * cq), kl1 = __shfl_sync(FULL, rows.kl, 2 * cq + 1);
       float* const out0 = logits + (size_t)ra * stride;
       ok = mq_segments(rows, R, qb, c, [&](const MqSegment& g) {
@@ -452,17 +461,25 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
           const int a = ea;
           if (kb * MQ_KEYS + 32 * qd < lim) {  // some lane of the warp stores
             const float scale = reinterpret_cast<const float*>(sgen + (scbuf - sbase) + est * MQ_SCBYTES)[32 * qd + l];
-            float v[2][32];
-            tc_ld32(tmem + a * MQ_N + ((uint32_t)(32 * qd) << 16) + 2 * cq * IH, v[0]);
-            tc_ld32(tmem + a * MQ_N + ((uint32_t)(32 * qd) << 16) + (2 * cq + 1) * IH, v[1]);
             // sum over heads of w * relu(v) for both rows at once: two chains of packed FMAs (even and
-            // odd heads), each lane holding (row ra, row ra + 1)
+            // odd heads), each lane holding (row ra, row ra + 1); heads 0 .. 15, then 16 .. 31
+            const uint32_t t0 = tmem + a * MQ_N + ((uint32_t)(32 * qd) << 16) + 2 * cq * IH;
             float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int h = 0; h < IH; h += 2) {
-              const float4 ww = *reinterpret_cast<const float4*>(wsm + 2 * h);  // w[ra][h], w[ra+1][h], .. h + 1
-              acc0 = fma2(make_float2(ww.x, ww.y), make_float2(relu_s(v[0][h]), relu_s(v[1][h])), acc0);
-              acc1 = fma2(make_float2(ww.z, ww.w), make_float2(relu_s(v[0][h + 1]), relu_s(v[1][h + 1])), acc1);
+            for (int half = 0; half < 2; ++half) {
+              uint32_t u0[16], u1[16];
+              tc_ld16_issue(t0 + 16 * half, u0);
+              tc_ld16_issue(t0 + IH + 16 * half, u1);
+              tc_ld16_wait(u0);
+              tc_ld16_after(u1);
+#pragma unroll
+              for (int h = 0; h < 16; h += 2) {
+                const float4 ww = half == 0 ? wr[h / 2] : *reinterpret_cast<const float4*>(wsm + 2 * (16 + h));
+                acc0 = fma2(make_float2(ww.x, ww.y),
+                            make_float2(relu_s(__uint_as_float(u0[h])), relu_s(__uint_as_float(u1[h]))), acc0);
+                acc1 = fma2(make_float2(ww.z, ww.w),
+                            make_float2(relu_s(__uint_as_float(u0[h + 1])), relu_s(__uint_as_float(u1[h + 1]))), acc1);
+              }
             }
             const float2 sum = make_float2(__fadd_rn(acc0.x, acc1.x), __fadd_rn(acc0.y, acc1.y));
             // streaming stores: the logits pass through L2 without evicting the keys the other row
