@@ -55,7 +55,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
-    ap.add_argument("--no-next-rows", action="store_true", help="skip timing the ops beside the path (q_post, add_rms_quant, quant, MQA logits)")
+    ap.add_argument("--no-next-rows", action="store_true",
+                    help="skip timing the ops beside the path (q_post, add_rms_quant, quant, MQA logits)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     return ap.parse_args()
 
