@@ -199,3 +199,26 @@ def test_mqa_logits_full_size_cfg3(cuda):
         worst = max(worst, float(err.max()))
         assert err.max() <= TOL, f"row {r} position {int(err.argmax())}"
     print(f"cfg3: {len(rows)} rows up to {int(klen[rows].max())} keys, worst error {worst:.3g} of magnitude")
+
+
+def test_mqa_logits_rows_without_keys(cuda):
+    """Rows whose klen is 0 (no key yet) get no logits and leave the other rows of their block
+    untouched; a launch where no row has a key writes nothing and flags nothing."""
+    import glmkv
+
+    case = _case([150, 0, 300], [12, 9, 7], seed=86)
+    call, pool, iq, w, row_seq, klen = case
+    klen = klen.copy()
+    klen[[0, 5, 12, 13, 27]] = 0  # inside a block, a block's first row, a sequence's first rows, the last row
+    R, stride = len(row_seq), 320
+    got = _run(cuda, call, pool, iq, w, row_seq, klen, stride)
+    from oracle import mqa
+    want = mqa.mqa_logits_paged(iq, pool, call.block_table, call.max_pages, row_seq, klen, w)
+    for r, (lg, mg) in enumerate(want):
+        k = int(klen[r])
+        assert np.all(np.isnan(got[r, k:])), r
+        if k:
+            err = np.abs(got[r, :k].astype(np.float64) - lg) / np.maximum(mg, 1e-30)
+            assert err.max() <= TOL, r
+    none = _run(cuda, call, pool, iq, w, row_seq, np.zeros_like(klen), stride)
+    assert np.all(np.isnan(none))
