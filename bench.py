@@ -56,7 +56,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--no-next-rows", action="store_true",
-                    help="skip timing the ops beside the path (q_post, add_rms_quant, quant, MQA logits)")
+                    help="skip timing the ops beside the path (q_post, add_rms_quant, quant, MQA logits) "
+                         "and the bf16-cache path")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     return ap.parse_args()
 
@@ -175,9 +176,9 @@ def layer_inputs(torch, group, T, gen):
     return out
 
 
-def topk_picks(torch, call, group, gen):
-    """Per indexer layer: 2048 positions uniform in [0, klen) per row (drawn with replacement on the
-    device), or 0 .. klen - 1 then -1 when klen <= 2048."""
+def topk_picks(torch, call, group, gen, layers=None):
+    """Per indexer layer (of `layers`, default the group's): 2048 positions uniform in [0, klen) per row
+    (drawn with replacement on the device), or 0 .. klen - 1 then -1 when klen <= 2048."""
     from glmkv import workload as W
     from glmkv.stage import FULL
 
@@ -186,7 +187,7 @@ def topk_picks(torch, call, group, gen):
     ar = torch.arange(2048, device=dev)
     short = (ar[None, :] < klen[:, None]).to(torch.int32) * (ar[None, :].to(torch.int32) + 1) - 1
     out = {}
-    for l in group.layers:
+    for l in (group.layers if layers is None else layers):
         if l not in FULL:
             continue
         pick = (torch.rand(call.T, 2048, device=dev, generator=gen) * klen[:, None]).to(torch.int32)
@@ -301,6 +302,82 @@ def next_rows(torch, impl, T, dev, reps=10):
         rows[name] = {"rows": T, "us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1), "algorithmic_bytes": nbytes}
     rows["glm_quant"]["K"] = K
     return rows
+
+
+def bf16_rows(torch, impl, group, meta, call, dev, reps=10):
+    """The bf16-cache path of the manifest (`--kv bf16`, gen.py:53): the append into a bf16 latent cache
+    (glm_mla_prep) on an indexer and a shared layer of the call, and the picks mapped to cache slots
+    through the page table (glm_topk_slots). glm_topk_slots rewrites its picks in place, so each of its
+    launches gets fresh picks copied in before its own events; the appends are timed as a run of
+    `reps` launches."""
+    from glmkv import traffic
+    from glmkv.stage import FULL
+
+    layers = [l for l in group.layers if l in FULL]
+    if not layers:
+        return {"unavailable": "no indexer layer in this stage"}
+    import glmkv
+    T = call.T
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(T, 2752, device=dev, generator=g).to(torch.bfloat16)
+    u = lambda n: (torch.rand(n, device=dev, generator=g) + 0.5).to(torch.bfloat16)
+    g_q, g_kv, ik_w = u(2048), u(512), u(128)
+    ik_b = (torch.randn(128, device=dev, generator=g) * 0.1).to(torch.bfloat16)
+    kvb = torch.empty(call.n_pages * 64 * 1152, dtype=torch.uint8, device=dev)
+    idx = group.idx[layers[0]]
+    picks = topk_picks(torch, call, group, g, layers[:1])[layers[0]]
+    ind = torch.empty_like(picks)
+    p = lambda t: t.data_ptr()
+    if impl == "glmkv":
+        def prep(full):
+            if full:
+                glmkv.mla_prep_full(x, 2752, g_q, g_kv, group.rope, group.pos, meta.slot, kvb, idx, ik_w, ik_b,
+                                    group.qq, group.qsf, group.sf_rows, T, kv_dtype="bf16")
+            else:
+                glmkv.mla_prep_shared(x, 2752, g_q, g_kv, group.rope, group.pos, meta.slot, kvb, group.qq,
+                                      group.qsf, group.sf_rows, T, kv_dtype="bf16")
+        slots = lambda: glmkv.topk_slots(ind, meta.block_table, call.max_pages, group.row_seq, group.klen,
+                                         group.tlen, T)
+    else:
+        from oracle import ref
+
+        def prep(full):
+            ref.mla_prep(False, p(x), 2752, p(g_q), p(g_kv), p(group.rope), p(group.pos), p(meta.slot), p(kvb),
+                         p(idx) if full else None, p(ik_w) if full else None, p(ik_b) if full else None,
+                         p(group.qq), p(group.qsf), group.sf_rows, T)
+        slots = lambda: ref.topk_slots(p(ind), p(meta.block_table), call.max_pages, p(group.row_seq),
+                                       p(group.klen), p(group.tlen), T)
+    out = {}
+    for full in (True, False):
+        for _ in range(2):
+            prep(full)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(reps):
+            prep(full)
+        e.record()
+        torch.cuda.synchronize()
+        us = s.elapsed_time(e) / reps * 1e3
+        nbytes = traffic.mla_prep(T, full, "bf16")
+        out["indexer_layer" if full else "shared_layer"] = {"us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1),
+                                                            "algorithmic_bytes": nbytes}
+    total = 0.0
+    for i in range(reps + 2):
+        ind.copy_(picks)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        slots()
+        e.record()
+        torch.cuda.synchronize()
+        if i >= 2:
+            total += s.elapsed_time(e) * 1e3
+    us = total / reps
+    nbytes = traffic.topk(T)
+    del x, kvb, picks, ind
+    return {"glm_mla_prep": {"rows": T, "kv_cache": "bf16 (1152 B/token)", **out},
+            "glm_topk_slots": {"rows": T, "us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1),
+                               "algorithmic_bytes": nbytes}}
 
 
 def mqa_row(torch, impl, group, meta, call, dev, reps=3, sub=1024):
@@ -574,6 +651,7 @@ def main():
     if not a.no_next_rows:
         line["next_rows"] = next_rows(torch, a.impl, call.T, dev)
         line["next_rows"]["glm_mqa_logits_paged"] = mqa_row(torch, a.impl, group, meta, call, dev)
+        line["next_rows"]["bf16_cache_path"] = bf16_rows(torch, a.impl, group, meta, call, dev)
     if a.impl == "reference":
         line["cpu_baseline"] = {"value": line["value"], "unit": "GB/s", "cores": 1, "kind": "reference",
                                 "sample": "the whole workload: the reference's glue kernels (kern-glm53 "
