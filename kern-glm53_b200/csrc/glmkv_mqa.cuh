@@ -18,9 +18,11 @@
 //    tcgen05.mma kind::f8f6f4 (e4m3 x e4m3 -> f32), M = 128 keys x N = 256 (row, head) x K = 128
 //    (four K = 32 steps) into one of two TMEM accumulators, and commits each stage and accumulator
 //    back to its barrier;
-//  - warps 2..17: the epilogue. Warp w reads TMEM lanes 32 (w % 4) .. + 31 (one key a thread) and
-//    the 64 columns of two query rows, then relu, the head-weighted sum and the key's scale, and
-//    stores the logits (32 consecutive keys a warp: 128-byte coalesced rows).
+//  - warps 2..17: the epilogue, in two groups of 8 that take the tiles of even and odd index (the
+//    two accumulators) so that their load and arithmetic phases interleave. Warp w reads TMEM lanes
+//    32 (w % 4) .. + 31 (one key a thread) and the columns of four query rows, two at a time, then
+//    relu, the head-weighted sum and the key's scale, and stores the logits (32 consecutive keys a
+//    warp: 128-byte coalesced rows).
 // A block of rows that spans two sequences is worked as two segments over the same query stage.
 // Every wait is bounded; a wait that gives up sets the fault word, stops every role, waits for the
 // copies and MMAs in flight and frees TMEM before returning.
@@ -45,7 +47,7 @@ constexpr int MQ_SCBYTES = MQ_KEYS * 4;          // 512 B: its keys' f32 scales
 constexpr int MQ_EPI_WARPS = 16;                 // four a TMEM lane quarter, two query rows each
 constexpr int MQ_THREADS = 32 * (2 + MQ_EPI_WARPS);
 constexpr int MQ_TMEM_COLS = 2 * MQ_N;           // two f32 accumulators of 256 columns
-constexpr int MQ_WBYTES = MQ_EPI_WARPS * 2 * IH * 4;  // each epilogue warp's two rows of head weights
+constexpr int MQ_WBYTES = MQ_EPI_WARPS * 4 * IH * 4;  // each epilogue warp's four rows of head weights
 constexpr int MQ_QTAB = 4096;                    // blocks whose largest klen is kept in shared memory
 // A key stage's descriptor word, written by the producer before the stage's copies: the first tile
 // of a work item (the MMA issuer then waits for the item's query stage), or the end of the launch.
@@ -97,7 +99,8 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
 // tc_ld16_after), so that no read of them moves above the wait.
 __device__ __forceinline__ void tc_ld16_issue(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
         "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
@@ -241,11 +244,11 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
       mbar_init(smem_u32(&q_full[i]), 1);
       mbar_init(smem_u32(&q_empty[i]), 1);
       mbar_init(smem_u32(&acc_full[i]), 1);
-      mbar_init(smem_u32(&acc_empty[i]), MQ_EPI_WARPS);
+      mbar_init(smem_u32(&acc_empty[i]), MQ_EPI_WARPS / 2);  // the group of that parity
     }
     for (int i = 0; i < MQ_KSTAGES; ++i) {
       mbar_init(smem_u32(&k_full[i]), 1);
-      mbar_init(smem_u32(&k_empty[i]), 1 + MQ_EPI_WARPS);  // the MMAs, and every epilogue warp at the tile's end
+      mbar_init(smem_u32(&k_empty[i]), 1 + MQ_EPI_WARPS / 2);  // the MMAs, and the group's warps at the tile's end
     }
     mbar_init(smem_u32(&mma_done), 1);
     mbar_init_fence();
@@ -418,84 +421,103 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
     }
   } else {
     // ---------------------------------------------------------------- epilogue: TMEM -> logits
-    const int qd = warp & 3, cq = (warp - 2) >> 2;  // TMEM lane quarter; query rows 2 cq, 2 cq + 1 of a block
-    float* wsm = reinterpret_cast<float*>(sgen + (wbuf - sbase)) + (warp - 2) * 2 * IH;
-    uint32_t est = 0, ea = 0, eph = 0;  // key stage, accumulator and its phase of the next tile
+    // Two groups of 8 warps: group gp works the tiles of parity gp (accumulator gp), so the groups'
+    // load and arithmetic phases interleave. Warp e of a group: TMEM lane quarter warp % 4, query rows
+    // 4 cq .. 4 cq + 3 of a block (two pairs).
+    const int e = warp - 2, gp = e >> 3;
+    const int qd = warp & 3, cq = (e & 7) >> 2;
+    float* wsm = reinterpret_cast<float*>(sgen + (wbuf - sbase)) + e * 4 * IH;
+    uint32_t est = 0, tpar = 0, eph = 0;  // key stage and parity of the next tile; the group accumulator's phase
     bool ok = true;
-    // this lane's share of a block's head weights: row 2 cq + (l >> 4), heads 2 (l & 15) and + 1
-    auto load_w = [&](int qb) {
-      const int r = qb * MQ_ROWS + 2 * cq + (l >> 4);
-      return r < R ? __ldg(reinterpret_cast<const float2*>(w + (size_t)r * IH + 2 * (l & 15))) : make_float2(0.f, 0.f);
-    };
     MqItems it(nqb, nch);
     mq_skip_empty(it, qmax, klen, R);
     while (ok && it.valid()) {
       const int qb = it.qb, c = it.c;
       const MqRows rows = mq_load_rows(row_seq, klen, R, qb);
-      const float2 wv = load_w(qb);
-      const int ra = qb * MQ_ROWS + 2 * cq;  // this warp's rows ra, ra + 1
-      // their head weights (zero past R), interleaved by head into the warp's shared-memory slice:
-      // wsm[2 h + j] = w[ra + j][h], so one packed FMA takes head h of both rows
-      __syncwarp();
-      {
-        const int j = l >> 4, h2 = 2 * (l & 15);
-        wsm[2 * h2 + j] = wv.x * 33554432.f;  // w * 2^25 (exact): relu(x) * w = relu_s(x) * (w * 2^25)
-        wsm[2 * h2 + 2 + j] = wv.y * 33554432.f;
+      const int r4 = qb * MQ_ROWS + 4 * cq;  // this warp's rows r4 .. r4 + 3
+      {  // head weights (zero past R) x 2^25, pair j interleaved by head: wsm[64 j + 2 h + i] = w[r4 + 2 j + i][h]
+        const int rr = l >> 3, h4 = 4 * (l & 7);
+        const float4 v = r4 + rr < R ? __ldg(reinterpret_cast<const float4*>(w + (size_t)(r4 + rr) * IH + h4))
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+        float* d = wsm + 64 * (rr >> 1) + (rr & 1);
+        __syncwarp();
+        d[2 * h4] = v.x * 33554432.f;  // w * 2^25 (exact): relu(x) * w = relu_s(x) * (w * 2^25)
+        d[2 * h4 + 2] = v.y * 33554432.f;
+        d[2 * h4 + 4] = v.z * 33554432.f;
+        d[2 * h4 + 6] = v.w * 33554432.f;
+        __syncwarp();
       }
-      __syncwarp();
-      float4 wr[8];  // heads 0 .. 15 of both rows, held in registers for the item
+      int klr[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) wr[i] = *reinterpret_cast<const float4*>(wsm + 4 * i);
-      const int kl0 = __shfl_sync(FULL, rows.kl, 2 * cq), kl1 = __shfl_sync(FULL, rows.kl, 2 * cq + 1);
-      float* const out0 = logits + (size_t)ra * stride;
+      for (int i = 0; i < 4; ++i) klr[i] = __shfl_sync(FULL, rows.kl, 4 * cq + i);
+      float* const out0 = logits + (size_t)r4 * stride;
       ok = mq_segments(rows, R, qb, c, [&](const MqSegment& g) {
         // the positions each row stores: below its klen and the stride, in its own segment only
-        const int lim0 = ra >= g.sb && ra < g.se ? min(kl0, stride) : 0;
-        const int lim1 = ra + 1 >= g.sb && ra + 1 < g.se ? min(kl1, stride) : 0;
-        const int lim = max(lim0, lim1);
+        int lim[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) lim[i] = r4 + i >= g.sb && r4 + i < g.se ? min(klr[i], stride) : 0;
+        const int limp0 = max(lim[0], lim[1]), limp1 = max(lim[2], lim[3]);
         for (int kb = g.kb0; kb < g.kb1; ++kb) {
-          const bool okw = mq_wait(smem_u32(&acc_full[ea]), eph, abort);
+          const uint32_t st = est;
+          const bool mine = tpar == (uint32_t)gp;
+          if (++est == MQ_KSTAGES) est = 0;
+          tpar ^= 1;
+          if (!mine) continue;  // the other group's tile
+          const bool okw = mq_wait(smem_u32(&acc_full[gp]), eph, abort);
           if (__any_sync(FULL, !okw)) return false;  // the warp leaves together: tcgen05.ld is warp-collective
           tc_fence_after();
           const int p = kb * MQ_KEYS + 32 * qd + l;  // this thread's key position
-          const int a = ea;
-          if (kb * MQ_KEYS + 32 * qd < lim) {  // some lane of the warp stores
-            const float scale = reinterpret_cast<const float*>(sgen + (scbuf - sbase) + est * MQ_SCBYTES)[32 * qd + l];
-            // sum over heads of w * relu(v) for both rows at once: two chains of packed FMAs (even and
-            // odd heads), each lane holding (row ra, row ra + 1); heads 0 .. 15, then 16 .. 31
-            const uint32_t t0 = tmem + a * MQ_N + ((uint32_t)(32 * qd) << 16) + 2 * cq * IH;
-            float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+          const int p0 = kb * MQ_KEYS + 32 * qd;
+          if (p0 < max(limp0, limp1)) {
+            const float scale = reinterpret_cast<const float*>(sgen + (scbuf - sbase) + st * MQ_SCBYTES)[32 * qd + l];
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-              uint32_t u0[16], u1[16];
-              tc_ld16_issue(t0 + 16 * half, u0);
-              tc_ld16_issue(t0 + IH + 16 * half, u1);
-              tc_ld16_wait(u0);
-              tc_ld16_after(u1);
+            for (int j = 0; j < 2; ++j) {
+              if (p0 >= (j ? limp1 : limp0)) continue;
+              // sum over heads of w * relu(v) for both rows of the pair: two chains of packed FMAs (even
+              // and odd heads), each lane holding (row 2 j, row 2 j + 1); heads 0 .. 15, then 16 .. 31
+              const uint32_t t0 = tmem + gp * MQ_N + ((uint32_t)(32 * qd) << 16) + (4 * cq + 2 * j) * IH;
+              const float* wp = wsm + 64 * j;
+              float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+              uint32_t ua[16], ub[16], va[16], vb[16];
+              tc_ld16_issue(t0, ua);
+              tc_ld16_issue(t0 + IH, ub);
+              tc_ld16_wait(ua);
+              tc_ld16_after(ub);
+              tc_ld16_issue(t0 + 16, va);  // the second half is on its way while the first is summed
+              tc_ld16_issue(t0 + IH + 16, vb);
 #pragma unroll
               for (int h = 0; h < 16; h += 2) {
-                const float4 ww = half == 0 ? wr[h / 2] : *reinterpret_cast<const float4*>(wsm + 2 * (16 + h));
+                const float4 ww = *reinterpret_cast<const float4*>(wp + 2 * h);
                 acc0 = fma2(make_float2(ww.x, ww.y),
-                            make_float2(relu_s(__uint_as_float(u0[h])), relu_s(__uint_as_float(u1[h]))), acc0);
+                            make_float2(relu_s(__uint_as_float(ua[h])), relu_s(__uint_as_float(ub[h]))), acc0);
                 acc1 = fma2(make_float2(ww.z, ww.w),
-                            make_float2(relu_s(__uint_as_float(u0[h + 1])), relu_s(__uint_as_float(u1[h + 1]))), acc1);
+                            make_float2(relu_s(__uint_as_float(ua[h + 1])), relu_s(__uint_as_float(ub[h + 1]))), acc1);
               }
+              tc_ld16_wait(va);
+              tc_ld16_after(vb);
+#pragma unroll
+              for (int h = 0; h < 16; h += 2) {
+                const float4 ww = *reinterpret_cast<const float4*>(wp + 2 * (16 + h));
+                acc0 = fma2(make_float2(ww.x, ww.y),
+                            make_float2(relu_s(__uint_as_float(va[h])), relu_s(__uint_as_float(vb[h]))), acc0);
+                acc1 = fma2(make_float2(ww.z, ww.w),
+                            make_float2(relu_s(__uint_as_float(va[h + 1])), relu_s(__uint_as_float(vb[h + 1]))), acc1);
+              }
+              const float2 sum = make_float2(__fadd_rn(acc0.x, acc1.x), __fadd_rn(acc0.y, acc1.y));
+              // streaming stores: the logits pass through L2 without evicting the keys the other row
+              // blocks of the sequence still read
+              float* const o = out0 + (size_t)(2 * j) * stride;
+              if (p < lim[2 * j]) __stcs(o + p, __fmul_rn(sum.x, scale));
+              if (p < lim[2 * j + 1]) __stcs(o + stride + p, __fmul_rn(sum.y, scale));
             }
-            const float2 sum = make_float2(__fadd_rn(acc0.x, acc1.x), __fadd_rn(acc0.y, acc1.y));
-            // streaming stores: the logits pass through L2 without evicting the keys the other row
-            // blocks of the sequence still read
-            if (p < lim0) __stcs(out0 + p, __fmul_rn(sum.x, scale));
-            if (p < lim1) __stcs(out0 + stride + p, __fmul_rn(sum.y, scale));
           }
           tc_fence_before();
           __syncwarp();
           if (l == 0) {  // the stage (its scales) and the accumulator are read
-            mbar_arrive(smem_u32(&k_empty[est]));
-            mbar_arrive(smem_u32(&acc_empty[ea]));
+            mbar_arrive(smem_u32(&k_empty[st]));
+            mbar_arrive(smem_u32(&acc_empty[gp]));
           }
-          if (++est == MQ_KSTAGES) est = 0;
-          ea ^= 1;
-          eph ^= ea ^ 1;  // the accumulator phase flips once both have been used
+          eph ^= 1;
         }
         return true;
       });
