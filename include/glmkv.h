@@ -52,8 +52,9 @@ int glmkv_plan(const int64_t* cu, const int32_t* seq_lens, int nseq, int32_t* po
  * source/glm_glue.cu:202-296). x [T, lda] bf16: q_a 2048 | kv_a 512 | k_pe 64 | wk 128; rope [pos][64]
  * bf16 (32 cos | 32 sin); slot [T] i64 (< 0: no cache write); idx, ik_w, ik_b all NULL on a shared
  * layer; qq [T, 2048] e4m3 out; qsf DeepGEMM-packed UE8M0 words [(2048 / 512)][sf_rows] out.
- * Needs lda % 4 == 0 and lda >= 2624 (2752 with idx), x 8-byte aligned, qq and qsf 4-byte aligned,
- * kv 16-byte aligned, sf_rows >= T. */
+ * Needs lda % 4 == 0 and lda >= 2624 (2752 with idx), x, g_q, ik_w and ik_b 8-byte aligned; g_kv,
+ * rope, qq, qsf, kv and idx 4-byte aligned (rows of x that are 16-byte aligned, lda % 8 == 0 and x
+ * 16-byte aligned, are staged by bulk copies, the others read directly); sf_rows >= T. */
 int glmkv_mla_prep(const void* x, int lda, const void* g_q, const void* g_kv, const void* rope, const int32_t* pos,
                    const int64_t* slot, void* kv, void* idx, const void* ik_w, const void* ik_b, void* qq, void* qsf,
                    int sf_rows, int T, glmkv_stream_t stream);

@@ -323,9 +323,11 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
         // lane j holds the page of position block 2 kb0 + j (the item's up to 32 pages)
         const int pj = 2 * g.kb0 + l;
         int pg = -1;
-        if (pj * PAGE < g.kmax && pj < max_pages) {
-          pg = block_table[(size_t)g.seq * max_pages + pj];
-          if (pg >= n_pages) pg = -1;
+        if (pj * PAGE < g.kmax) {  // a position the rows need: its page must be in the table and the pool
+          if (pj < max_pages) {
+            pg = block_table[(size_t)g.seq * max_pages + pj];
+            if (pg >= n_pages) pg = -1;
+          }
           if (pg < 0) atomicOr(&g_fault, FAULT_BAD_PAGE);
         }
         for (int kb = g.kb0; kb < g.kb1; ++kb) {
@@ -540,9 +542,10 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
 // cache pages (no gather). tm_q maps iq as [R * 32 rows][128 B] (box 256 rows, 128-byte swizzle);
 // tm_k maps the indexer cache as [pages][64 rows][128 B] with strides 8448 and 128 B (box one page,
 // 128-byte swizzle). idx is the same cache of n_pages pages (the key scales at each page's tail);
-// a block-table entry outside 0 .. n_pages - 1 is skipped and flagged. No counterpart
+// a block-table entry outside 0 .. n_pages - 1, or a key position past the table's max_pages pages,
+// is skipped and flagged (the logits of its keys are then not defined). No counterpart
 // among the glue kernels: it replaces the gather plus DeepGEMM's MQA logits.
-//   persistent: grid = SMs, block 576, dynamic smem MQ_SMEM (172,032 B)
+//   persistent: grid = SMs, block 576, dynamic smem MQ_SMEM (176,128 B)
 extern "C" __global__ void __launch_bounds__(glmkv::MQ_THREADS, 1)
     glm_mqa_logits_paged(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const glmkv::u8* __restrict__ idx, int n_pages, const int* __restrict__ block_table,

@@ -4,9 +4,11 @@
   ``-ffp-contract=off`` so every f32 rounding is the one written in the source).
 * ``oracle/_ref/libglmref.so``: the reference's own ``source/glm_glue.cu``, compiled unmodified from
   the reference tree for sm_100a with the host launchers in ``ref_launch.cu``. Built only where the
-  reference tree is present; the built library travels with the repository snapshot to the GPU box.
+  reference tree is given (``--ref-root`` or ``GLMKV_REFERENCE_ROOT``); the built library travels with
+  the repository snapshot to the GPU box.
 
-    python oracle/build.py [--ref-root PATH]
+    python oracle/build.py --ref-root path/to/kern-glm53
+    GLMKV_REFERENCE_ROOT=path/to/kern-glm53 python oracle/build.py
 """
 import argparse
 import os
@@ -19,7 +21,7 @@ BUILD = HERE / "_build"
 REF_OUT = HERE / "_ref"
 ORACLE_SO = BUILD / "libglmoracle.so"
 REF_SO = REF_OUT / "libglmref.so"
-DEFAULT_REF_ROOT = pathlib.Path(os.environ.get("GLMKV_REFERENCE_ROOT", "/root/reference"))
+ENV_REF_ROOT = "GLMKV_REFERENCE_ROOT"
 NVCC = os.environ.get("NVCC", shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc")
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -43,11 +45,22 @@ def build_oracle(force=False):
     return ORACLE_SO
 
 
-def build_ref(ref_root=DEFAULT_REF_ROOT, force=False):
-    """Compile the reference glue kernels from the reference tree; returns None when it is absent."""
-    glue = pathlib.Path(ref_root) / "source" / "glm_glue.cu"
-    if not glue.exists():
+def reference_root(ref_root=None):
+    """The kern-glm53 checkout: the argument, else GLMKV_REFERENCE_ROOT; None when neither is given."""
+    root = ref_root or os.environ.get(ENV_REF_ROOT)
+    return pathlib.Path(root) if root else None
+
+
+def build_ref(ref_root=None, force=False):
+    """Compile the reference glue kernels from the reference tree (the argument, else
+    GLMKV_REFERENCE_ROOT). Returns None when no tree is given; raises when the one given has no
+    source/glm_glue.cu."""
+    root = reference_root(ref_root)
+    if root is None:
         return None
+    glue = root / "source" / "glm_glue.cu"
+    if not glue.exists():
+        raise FileNotFoundError(f"{root} has no source/glm_glue.cu: not a kern-glm53 checkout")
     launch = HERE / "ref_launch.cu"
     if force or _stale(REF_SO, [glue, launch]):
         REF_OUT.mkdir(exist_ok=True)
@@ -61,10 +74,12 @@ def build_ref(ref_root=DEFAULT_REF_ROOT, force=False):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-root", default=str(DEFAULT_REF_ROOT))
+    ap.add_argument("--ref-root", default=None, help=f"the kern-glm53 checkout (default: ${ENV_REF_ROOT})")
     ap.add_argument("--force", action="store_true")
     a = ap.parse_args()
     print(build_oracle(a.force))
+    if reference_root(a.ref_root) is None:
+        raise SystemExit(f"the reference glue kernels need the kern-glm53 checkout: --ref-root or ${ENV_REF_ROOT}")
     print(build_ref(a.ref_root, a.force))
 
 

@@ -24,7 +24,8 @@ def lib():
     global _lib
     if _lib is None:
         if not _build.REF_SO.exists() and _build.build_ref() is None:
-            raise RefUnavailable(f"{_build.REF_SO} is missing and the reference tree is not present to build it")
+            raise RefUnavailable(f"{_build.REF_SO} is missing: build it with `python oracle/build.py --ref-root "
+                                 "<kern-glm53 checkout>`")
         _lib = ctypes.CDLL(str(_build.REF_SO))
         P, I = ctypes.c_void_p, ctypes.c_int
         _lib.ref_glm_plan.argtypes = [P, P, I, P, P, P, P, P, P, I, P]

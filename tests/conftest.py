@@ -33,3 +33,17 @@ def cuda(built_lib):
         pytest.fail("GPU test run without a CUDA device")
     torch.cuda.init()
     return torch.device("cuda:0")
+
+
+@pytest.fixture(scope="session")
+def ref(cuda):
+    """The reference's own glue kernels (oracle/_ref/libglmref.so), the bit-exact oracle of every GPU
+    parity test. A GPU run without them fails: the bit-exact half of the suite must not turn into
+    skips or looser oracle checks."""
+    from oracle import ref as ref_mod
+
+    if not ref_mod.available():
+        pytest.fail("oracle/_ref/libglmref.so is missing: build it with `python oracle/build.py --ref-root "
+                    "<kern-glm53 checkout>` where the reference tree is present; it travels with the repository")
+    ref_mod.lib()
+    return ref_mod

@@ -7,18 +7,19 @@ call on the ``glm_glue`` module, resolves list variables assigned in the same fu
 (``norm_params``, ``prep_params``) and the entry variable ``prep`` (both of its values), and writes
 ``manifest_params.json`` beside this file: op -> {entries, params, nulled, line}.
 
-    python tests/golden/make_manifest_params.py [path/to/kern-glm53]
+    python tests/golden/make_manifest_params.py path/to/kern-glm53
+    GLMKV_REFERENCE_ROOT=path/to/kern-glm53 python tests/golden/make_manifest_params.py
 
 The CPU test ``tests/test_manifest.py`` checks the C ABI header and the kernels' parameter lists
 against the committed JSON, so it runs where the reference tree is absent.
 """
 import ast
 import json
+import os
 import pathlib
 import sys
 
 HERE = pathlib.Path(__file__).resolve().parent
-DEFAULT_REF = pathlib.Path("/root/reference")  # the default location of the kern-glm53 checkout
 
 
 def literal(node, env):
@@ -67,7 +68,12 @@ def collect(tree):
 
 
 def main():
-    ref = pathlib.Path(sys.argv[1]) if len(sys.argv) > 1 else DEFAULT_REF
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GLMKV_REFERENCE_ROOT")
+    if not root:
+        raise SystemExit("give the kern-glm53 checkout as the argument or in GLMKV_REFERENCE_ROOT")
+    ref = pathlib.Path(root)
+    if not (ref / "scripts" / "gen.py").exists():
+        raise SystemExit(f"{ref} has no scripts/gen.py: not a kern-glm53 checkout")
     gen = ref / "scripts" / "gen.py"
     ops = collect(ast.parse(gen.read_text()))
     out = HERE / "manifest_params.json"

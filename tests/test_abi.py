@@ -16,6 +16,14 @@ def declared():
     return re.findall(r"^(?:int|const char\*)\s+(glmkv_\w+)\s*\(", text, flags=re.M)
 
 
+def _has_cuda_device():
+    try:
+        import torch
+        return torch.cuda.is_available()
+    except ImportError:
+        return False
+
+
 def test_header_declares_the_manifest_ops():
     names = set(declared())
     assert {"glmkv_plan", "glmkv_mla_prep", "glmkv_mla_prep_fp8", "glmkv_idx_gather", "glmkv_kv_dequant",
@@ -57,6 +65,16 @@ def test_host_side_argument_checks(built_lib):
         assert fn(*bad) == _lib.OK                                                      # T = 0
         shared = list(args); shared[1] = 2624; shared[8] = shared[9] = shared[10] = None; shared[14] = -1
         assert fn(*shared) == _lib.ERR_ARG                                              # T < 0
+        # the latent cache kv needs 4-byte alignment (include/glmkv.h): 4 passes the host checks and
+        # reaches the device query, which fails without a GPU (never run where a device exists: the
+        # addresses are not real); 2 is rejected
+        if not _has_cuda_device():
+            ok4 = list(args); ok4[7] = A + 4
+            assert fn(*ok4) == _lib.ERR_DEVICE
+        bad = list(args); bad[7] = A + 2
+        assert fn(*bad) == _lib.ERR_ALIGN
+        bad = list(args); bad[8] = A + 2
+        assert fn(*bad) == _lib.ERR_ALIGN                                               # idx 4-byte
     assert L.glmkv_kv_dequant(A + 8, A, 16, A, 1, A, None) == _lib.ERR_ALIGN
     assert L.glmkv_kv_dequant(A, A, 16, A, 1, A + 8, None) == _lib.ERR_ALIGN
     assert L.glmkv_kv_dequant(A, A, 16, A, -1, A, None) == _lib.ERR_ARG

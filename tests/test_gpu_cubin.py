@@ -11,7 +11,13 @@ torch = pytest.importorskip("torch")
 
 CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES = 8
 ENTRIES = ("glm_plan", "glm_mla_prep", "glm_mla_prep_fp8", "glm_idx_gather", "glm_kv_dequant", "glm_topk_stream",
-           "glm_topk_slots", "glm_q_post", "glm_add_rms_quant", "glm_quant")
+           "glm_topk_slots", "glm_q_post", "glm_add_rms_quant", "glm_quant", "glm_mqa_logits_paged")
+
+
+class TensorMap(ctypes.Structure):
+    """CUtensorMap: 128 opaque bytes, 64-byte aligned, passed to a kernel by value."""
+    _align_ = 64
+    _fields_ = [("opaque", ctypes.c_uint64 * 16)]
 
 
 class Driver:
@@ -34,10 +40,23 @@ class Driver:
         if smem > 0:  # dynamic plus static shared memory above 48 KB needs the opt-in
             self._ok(self.cu.cuFuncSetAttribute(f, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, ctypes.c_int(smem)),
                      "cuFuncSetAttribute")
-        vals = [ctypes.c_uint64(a) if isinstance(a, PtrArg) else ctypes.c_int(a) for a in args]
+        vals = [a if isinstance(a, TensorMap) else ctypes.c_uint64(a) if isinstance(a, PtrArg) else ctypes.c_int(a)
+                for a in args]
         arr = (ctypes.c_void_p * len(vals))(*[ctypes.cast(ctypes.byref(v), ctypes.c_void_p) for v in vals])
         stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
         self._ok(self.cu.cuLaunchKernel(f, grid, 1, 1, block, 1, 1, smem, stream, arr, None), f"cuLaunchKernel {name}")
+
+    def tensor_map_u8(self, base, dims, strides, box):
+        """A tiled u8 tensor map with the 128-byte swizzle and 256-byte L2 promotion, as the library's
+        launcher of glm_mqa_logits_paged encodes it (csrc/glmkv.cu)."""
+        tm = TensorMap()
+        n = len(dims)
+        u64, u32 = ctypes.c_uint64, ctypes.c_uint32
+        rc = self.cu.cuTensorMapEncodeTiled(ctypes.byref(tm), 0, n, ctypes.c_void_p(base), (u64 * n)(*dims),
+                                            (u64 * (n - 1))(*strides), (u32 * n)(*box), (u32 * n)(*([1] * n)), 0, 3, 3,
+                                            0)
+        self._ok(rc, "cuTensorMapEncodeTiled")
+        return tm
 
     def close(self):
         self.cu.cuModuleUnload(self.mod)
@@ -157,3 +176,94 @@ def test_cubin_glue_entries_match_the_library(cuda):
             assert np.array_equal(a, b), "quant"
     finally:
         drv.close()
+
+
+def test_cubin_mqa_logits_matches_the_library(cuda):
+    """glm_mqa_logits_paged from the cubin, with tensor maps encoded through the driver API as a kern
+    manifest would and the launch shape glmkv_launch_shape reports: the same logits as
+    the library's launcher."""
+    import glmkv
+    from glmkv import workload as W
+
+    rng = np.random.default_rng(91)
+    call = W.make_call([300, 0, 70], [40, 21, 9], rng, spare_pages=3)
+    codes = rng.integers(0, 256, size=call.n_pages * 64 * 132, dtype=np.uint8)
+    codes = np.where((codes & 0x7F) == 0x7F, codes - 1, codes).astype(np.uint8)
+    pool = codes.reshape(call.n_pages, 64 * 132)
+    pool[:, 8192:] = np.exp2(rng.integers(-8, 4, size=(call.n_pages, 64))).astype(np.float32).view(np.uint8)
+    R = call.T
+    iq = rng.integers(0, 126, size=R * 32 * 128, dtype=np.uint8)
+    w = rng.standard_normal((R, 32)).astype(np.float32)
+    row_seq = np.repeat(np.arange(call.nseq, dtype=np.int32), call.fresh)
+    klen = (W.positions(call) + 1).astype(np.int32)
+    stride = int(klen.max())
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    iq_d, pool_d, bt_d, rs_d, kl_d, w_d = t(iq), t(pool.reshape(-1)), t(call.block_table), t(row_seq), t(klen), t(w)
+    outs = []
+    drv = Driver(glmkv.CUBIN_PATH)
+    try:
+        for via in ("lib", "cubin"):
+            logits = torch.full((R * stride,), float("nan"), dtype=torch.float32, device=cuda)
+            if via == "lib":
+                glmkv.mqa_logits_paged(iq_d, pool_d, call.n_pages, bt_d, call.max_pages, rs_d, kl_d, w_d, logits,
+                                       stride, R)
+            else:
+                tm_q = drv.tensor_map_u8(iq_d.data_ptr(), [128, R * 32], [128], [128, 256])
+                tm_k = drv.tensor_map_u8(pool_d.data_ptr(), [128, 64, call.n_pages], [128, 8448], [128, 64, 1])
+                g, b, sm = glmkv.launch_shape("glm_mqa_logits_paged", R)
+                drv.launch("glm_mqa_logits_paged", g, b, sm,
+                           [tm_q, tm_k, P(pool_d), call.n_pages, P(bt_d), call.max_pages, P(rs_d), P(kl_d), P(w_d),
+                            P(logits), stride, R])
+            torch.cuda.synchronize()
+            outs.append(logits.cpu().numpy())
+    finally:
+        drv.close()
+    assert glmkv.fault_flags() == 0
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    assert np.isfinite(outs[0].reshape(R, stride)[0, :klen[0]]).all()
+
+
+def _snippet_shapes():
+    """(entry, grid expression, block, dynamic shared memory) of every launch in INTEGRATION.md's
+    manifest snippets."""
+    import pathlib
+    import re
+
+    text = (pathlib.Path(__file__).resolve().parents[1] / "INTEGRATION.md").read_text()
+    out = []
+    for m in re.finditer(r'G\.b200\((?:"(glm_\w+)"|prep), \w+, \[(.+?), 1, 1\], \[(\d+), 1, 1\](?:, (\d+))?', text):
+        entries = [m.group(1)] if m.group(1) else ["glm_mla_prep_fp8", "glm_mla_prep"]
+        for e in entries:
+            out.append((e, m.group(2), int(m.group(3)), int(m.group(4) or 0)))
+    for m in re.finditer(r'launch\("glm_glue_b200", "(glm_\w+)", \[(.+?), 1, 1\], \[(\d+), 1, 1\],\s*(\d+)', text):
+        out.append((m.group(1), m.group(2), int(m.group(3)), int(m.group(4))))
+    return out
+
+
+def test_integration_snippet_matches_the_launch_shapes(cuda):
+    """Every launch of INTEGRATION.md's manifest snippets uses the block and dynamic shared memory the
+    library launches that entry with, and (with the device's SM count for SMS_B200 and T = 16,384) its
+    grid. A snippet that gave a kernel less shared memory than it uses would corrupt its results."""
+    import re
+
+    import glmkv
+
+    T = 16384
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    shapes = _snippet_shapes()
+    assert {e for e, *_ in shapes} == set(ENTRIES), sorted({e for e, *_ in shapes})
+
+    def grid_of(expr):
+        expr = expr.strip().replace("G.SMS_B200", "SMS").replace("SMS_B200", "SMS")
+        m = re.fullmatch(r'\{"ceil_div": \[(\w+), (\d+)\]\}', expr)
+        if m:
+            return -(-{"T": T}[m.group(1)] // int(m.group(2)))
+        return eval(expr, {"SMS": sms, "T": T})
+
+    for entry, grid, block, smem in shapes:
+        if entry == "glm_quant":  # its grid depends on K as well: block 256, no shared memory
+            assert (block, smem) == (256, 0), entry
+            continue
+        g, b, s = glmkv.launch_shape(entry, T)
+        assert (block, smem) == (b, s), f"{entry}: snippet block {block} smem {smem}, library {b} {s}"
+        assert grid_of(grid) == g, f"{entry}: snippet grid {grid} = {grid_of(grid)}, library {g}"

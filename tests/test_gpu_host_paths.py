@@ -35,14 +35,11 @@ def _many_seq_call(n, seed):
 
 
 @pytest.mark.parametrize("nseq", [257, 300])
-def test_more_sequences_than_staged(cuda, nseq):
+def test_more_sequences_than_staged(cuda, ref, nseq):
     """More than 256 sequences: glm_plan continues its scan in global memory; the page cursors walk
     hundreds of sequences. Bit-exact against the reference."""
     from layer_case import LayerCase, run_glmkv, run_reference
-    from oracle import ref
 
-    if not ref.available():
-        pytest.skip("reference library not built")
     case = LayerCase(_many_seq_call(nseq, nseq), "fp8", seed=nseq, with_topk=True)
     a, b = case.device(torch, cuda), case.device(torch, cuda)
     run_glmkv(case, a, full=True)
@@ -53,15 +50,12 @@ def test_more_sequences_than_staged(cuda, nseq):
         assert_equal(ga[k].view(np.uint8), gb[k].view(np.uint8), f"{nseq} sequences: {k}")
 
 
-def test_layer_group_matches_reference_layer_by_layer(cuda):
+def test_layer_group_matches_reference_layer_by_layer(cuda, ref):
     """LayerGroup.run_call over layers 0..6 (indexer layers 0, 1, 2, 6 and shared 3, 4, 5) gives the
     caches, streams and row plans of the reference kernels run in the manifest's order."""
     import glmkv
     from glmkv import stage, workload as W
-    from oracle import ref
 
-    if not ref.available():
-        pytest.skip("reference library not built")
     call = W.config("cfg0", seed=21)
     rng = np.random.default_rng(21)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)

@@ -222,3 +222,58 @@ def test_mqa_logits_rows_without_keys(cuda):
             assert err.max() <= TOL, r
     none = _run(cuda, call, pool, iq, w, row_seq, np.zeros_like(klen), stride)
     assert np.all(np.isnan(none))
+
+
+def test_mqa_logits_partial_block_and_empty_segment(cuda):
+    """R not a multiple of 8 (the last block's query tile is zero-filled past R), and blocks whose rows
+    span two sequences where one whole segment has klen 0. Nothing is written for rows past R (a NaN
+    guard region after the last row stays NaN) or for the empty segment's rows."""
+    import glmkv
+
+    case = _case([40, 0, 200], [5, 6, 10], seed=87)
+    call, pool, iq, w, row_seq, klen = case
+    klen = klen.copy()
+    klen[row_seq == 1] = 0  # rows 5 .. 10: the second segment of block 0 and the first of block 1
+    R, stride = len(row_seq), 224
+    assert R % 8 != 0
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    logits = torch.full(((R + 8) * stride,), float("nan"), dtype=torch.float32, device=cuda)
+    glmkv.mqa_logits_paged(t(iq), t(pool), call.n_pages, t(call.block_table), call.max_pages, t(row_seq), t(klen),
+                           t(w), logits, stride, R)
+    torch.cuda.synchronize()
+    assert glmkv.fault_flags() == 0
+    got = logits.cpu().numpy().reshape(R + 8, stride)
+    assert np.all(np.isnan(got[R:])), "logits written past the last row"
+    from oracle import mqa
+    want = mqa.mqa_logits_paged(iq, pool, call.block_table, call.max_pages, row_seq, klen, w)
+    for r, (lg, mg) in enumerate(want):
+        k = int(klen[r])
+        assert np.all(np.isnan(got[r, k:])), r
+        if k:
+            err = np.abs(got[r, :k].astype(np.float64) - lg) / np.maximum(mg, 1e-30)
+            assert err.max() <= TOL, r
+
+
+def test_mqa_logits_keys_past_the_block_table_are_flagged(cuda):
+    """Rows whose klen reaches past the block table's max_pages pages: those key pages are not read
+    (no entry exists for them) and the launch sets fault bit 2; positions inside the table stay exact."""
+    import glmkv
+
+    case = _case([300], [20], seed=88)
+    call, pool, iq, w, row_seq, klen = case
+    mp = 3  # pages 0 .. 2 (positions < 192) of a sequence that reaches position 319
+    bt = np.ascontiguousarray(call.block_table[:, :mp])
+    R, stride = len(row_seq), 320
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    logits = torch.full((R * stride,), float("nan"), dtype=torch.float32, device=cuda)
+    glmkv.fault_flags(clear=True)
+    glmkv.mqa_logits_paged(t(iq), t(pool), call.n_pages, t(bt), mp, t(row_seq), t(klen), t(w), logits, stride, R)
+    torch.cuda.synchronize()
+    assert glmkv.fault_flags(clear=True) & 2
+    got = logits.cpu().numpy().reshape(R, stride)
+    from oracle import mqa
+    want = mqa.mqa_logits_paged(iq, pool, call.block_table, call.max_pages, row_seq, klen, w)
+    for r, (lg, mg) in enumerate(want):
+        k = min(int(klen[r]), mp * 64)
+        err = np.abs(got[r, :k].astype(np.float64) - lg[:k]) / np.maximum(mg[:k], 1e-30)
+        assert err.max() <= TOL, r

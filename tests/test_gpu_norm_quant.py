@@ -34,15 +34,14 @@ CASES = [(1, True, True, True), (37, True, True, True), (512, True, True, True),
 
 
 @pytest.mark.parametrize("T,with_a,want_normed,want_q", CASES)
-def test_add_rms_quant_vs_reference_and_oracle(cuda, T, with_a, want_normed, want_q):
-    from oracle import cpu, ref
+def test_add_rms_quant_vs_reference_and_oracle(cuda, ref, T, with_a, want_normed, want_q):
+    from oracle import cpu
     a, res, gamma = _inputs(T, 1000 + T + 7 * with_a, with_a)
     got = _run("glmkv", a, res, gamma, T, want_normed, want_q, cuda)
-    if ref.available():
-        want = _run("reference", a, res, gamma, T, want_normed, want_q, cuda)
-        for k in got:
-            if got[k] is not None:
-                assert_equal(got[k].view(np.uint8), want[k].view(np.uint8), f"add_rms_quant vs reference: {k}")
+    want = _run("reference", a, res, gamma, T, want_normed, want_q, cuda)
+    for k in got:
+        if got[k] is not None:
+            assert_equal(got[k].view(np.uint8), want[k].view(np.uint8), f"add_rms_quant vs reference: {k}")
     r2 = res.copy()
     normed = np.zeros(T * H, np.uint16) if want_normed else None
     q = np.zeros(T * H, np.uint8) if want_q else None
@@ -59,10 +58,7 @@ def test_add_rms_quant_vs_reference_and_oracle(cuda, T, with_a, want_normed, wan
         assert_values_close(vals(got["q"], got["sf"]), vals(q, sf), E4M3_REL, "add_rms_quant vs oracle: q")
 
 
-def test_add_rms_quant_16384_rows_vs_reference(cuda):
-    from oracle import ref
-    if not ref.available():
-        pytest.skip("reference library not built")
+def test_add_rms_quant_16384_rows_vs_reference(cuda, ref):
     a, res, gamma = _inputs(16384, 5)
     got = _run("glmkv", a, res, gamma, 16384, True, True, cuda)
     want = _run("reference", a, res, gamma, 16384, True, True, cuda)
@@ -71,17 +67,15 @@ def test_add_rms_quant_16384_rows_vs_reference(cuda):
 
 
 @pytest.mark.parametrize("T,K,ldx", [(1, 128, 128), (37, 640, 648), (512, 16384, 16384), (16384, 16384, 16384)])
-def test_quant_vs_reference_and_oracle(cuda, T, K, ldx):
+def test_quant_vs_reference_and_oracle(cuda, ref, T, K, ldx):
     import glmkv
     from glmkv import workload as W
-    from oracle import cpu, ref
+    from oracle import cpu
     x = quant_case(T, K, ldx)
     dx = torch.from_numpy(x.view(np.int16)).to(cuda)
     sf_words = (K + 511) // 512
     outs = []
     for impl in ("glmkv", "reference"):
-        if impl == "reference" and not ref.available():
-            continue
         q = torch.zeros(T * K, dtype=torch.uint8, device=cuda)
         sf = torch.zeros(sf_words * T * 4, dtype=torch.uint8, device=cuda)
         if impl == "glmkv":
@@ -90,9 +84,8 @@ def test_quant_vs_reference_and_oracle(cuda, T, K, ldx):
             ref.quant(dx.data_ptr(), ldx, q.data_ptr(), sf.data_ptr(), T, K, T)
         torch.cuda.synchronize()
         outs.append((q.cpu().numpy(), sf.cpu().numpy()))
-    if len(outs) == 2:
-        assert_equal(outs[0][0], outs[1][0], "quant vs reference: q")
-        assert_equal(outs[0][1], outs[1][1], "quant vs reference: sf")
+    assert_equal(outs[0][0], outs[1][0], "quant vs reference: q")
+    assert_equal(outs[0][1], outs[1][1], "quant vs reference: sf")
     if T <= 512:
         q = np.zeros(T * K, np.uint8)
         sf = np.zeros(sf_words * T * 4, np.uint8)

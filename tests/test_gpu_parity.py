@@ -15,24 +15,16 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 
-def _ref_available():
-    from oracle import ref
-    return ref.available()
-
-
-needs_ref = pytest.mark.skipif(not _ref_available(), reason="oracle/_ref/libglmref.so not built (no reference tree)")
-
-
 def _run_both(case, cuda, full=True):
+    """The layer through libglmkv and through the reference kernels, on separate device copies."""
     import glmkv
 
     d_mine, d_ref = case.device(torch, cuda), case.device(torch, cuda)
     run_glmkv(case, d_mine, full)
-    if _ref_available():
-        run_reference(case, d_ref, full)
+    run_reference(case, d_ref, full)
     torch.cuda.synchronize()
     assert glmkv.fault_flags() == 0
-    return to_host(d_mine, torch), (to_host(d_ref, torch) if _ref_available() else None)
+    return to_host(d_mine, torch), to_host(d_ref, torch)
 
 
 def _assert_all_equal(got, want, what):
@@ -55,14 +47,13 @@ CASES = [
 
 
 @pytest.mark.parametrize("name,kv_dtype,full,zero_tiles", CASES)
-def test_layer_vs_reference_and_oracle(cuda, name, kv_dtype, full, zero_tiles):
+def test_layer_vs_reference_and_oracle(cuda, ref, name, kv_dtype, full, zero_tiles):
     from glmkv import workload as W
 
     call = W.config(name, seed=3)
     case = LayerCase(call, kv_dtype=kv_dtype, seed=11, zero_tiles=zero_tiles)
-    got, ref = _run_both(case, cuda, full)
-    if ref is not None:
-        _assert_all_equal(got, ref, f"{name}/{kv_dtype}/{'full' if full else 'shared'} vs reference")
+    got, want = _run_both(case, cuda, full)
+    _assert_all_equal(got, want, f"{name}/{kv_dtype}/{'full' if full else 'shared'} vs reference")
     h = case.host()
     run_oracle(case, h, full)
     for k in ("pos", "ks", "ke", "klen", "row_seq", "zero") + (("ind", "tlen") if full else ()):
@@ -84,7 +75,7 @@ def test_layer_vs_reference_and_oracle(cuda, name, kv_dtype, full, zero_tiles):
 
 
 @pytest.mark.parametrize("kv_dtype,full", [("fp8", True), ("fp8", False), ("bf16", True)])
-def test_append_padding_rows_skip_the_caches(cuda, kv_dtype, full):
+def test_append_padding_rows_skip_the_caches(cuda, ref, kv_dtype, full):
     """Rows with slot < 0 (padding) still get their q quant but write no cache row (glm_glue.cu:231-232):
     bit-exact against the reference, and the caches equal the oracle's everywhere else."""
     from glmkv import workload as W
@@ -94,9 +85,8 @@ def test_append_padding_rows_skip_the_caches(cuda, kv_dtype, full):
     call.slot_mapping[::7] = -1
     call.slot_mapping[-3:] = -1  # the last rows of the call, and so of the last warp's share
     case = LayerCase(call, kv_dtype=kv_dtype, seed=13)
-    got, ref = _run_both(case, cuda, full)
-    if ref is not None:
-        _assert_all_equal(got, ref, f"padding rows/{kv_dtype}/{'full' if full else 'shared'} vs reference")
+    got, want = _run_both(case, cuda, full)
+    _assert_all_equal(got, want, f"padding rows/{kv_dtype}/{'full' if full else 'shared'} vs reference")
     h = case.host()
     run_oracle(case, h, full)
     assert_prep_close(got, h, case, full, what="padding rows vs oracle")
@@ -112,12 +102,11 @@ def test_append_padding_rows_skip_the_caches(cuda, kv_dtype, full):
                      "indexer keys not written")
 
 
-@needs_ref
-def test_dequant_all_codes_vs_reference(cuda):
+def test_dequant_all_codes_vs_reference(cuda, ref):
     """Every e4m3 code (NaN included) and scales over 24 binades: identical bits to the reference."""
     from glmkv import workload as W
     import glmkv
-    from oracle import ref, cpu
+    from oracle import cpu
 
     call = W.config("cfg1", seed=5)
     case = LayerCase(call, seed=5, nan_codes=True, with_topk=False)
@@ -135,13 +124,11 @@ def test_dequant_all_codes_vs_reference(cuda):
     assert_equal(a, h, "kvd vs oracle")
 
 
-@needs_ref
 @pytest.mark.parametrize("op", ["kv_dequant", "idx_gather", "topk_stream", "plan"])
-def test_full_size_1m_context_vs_reference(cuda, op):
+def test_full_size_1m_context_vs_reference(cuda, ref, op):
     """cfg2: one sequence of 2^20 tokens (16,384 pages, a 1.2 GB bf16 stream), bit-exact on the device."""
     from glmkv import workload as W
     import glmkv
-    from oracle import ref
 
     c = W.config("cfg2", seed=7)
     g = torch.Generator(device=cuda).manual_seed(7)
@@ -188,16 +175,15 @@ def test_full_size_1m_context_vs_reference(cuda, op):
     assert _g.fault_flags() == 0
 
 
-@needs_ref
 @pytest.mark.parametrize("kv_dtype", ["fp8", "bf16"])
-def test_full_size_append_16384_rows_vs_reference(cuda, kv_dtype):
+def test_full_size_append_16384_rows_vs_reference(cuda, ref, kv_dtype):
     """cfg1's 16,384-row append on an indexer layer, bit-exact against the reference kernel."""
     from glmkv import workload as W
 
     call = W.config("cfg1", seed=9)
     case = LayerCase(call, kv_dtype=kv_dtype, seed=9, zero_tiles=32, with_topk=False)
-    got, ref = _run_both(case, cuda, full=True)
-    _assert_all_equal(got, ref, f"cfg1 append {kv_dtype}")
+    got, want = _run_both(case, cuda, full=True)
+    _assert_all_equal(got, want, f"cfg1 append {kv_dtype}")
 
 
 def test_append_then_dequant_round_trip(cuda):
@@ -269,9 +255,8 @@ def test_bad_page_is_skipped_and_flagged(cuda):
     assert torch.equal(s[hi:c.ctx].view(torch.int16), g[hi:c.ctx].view(torch.int16))
 
 
-@needs_ref
 @pytest.mark.parametrize("lda", [2756, 2760])
-def test_append_rows_not_aligned_for_bulk_copy(cuda, lda):
+def test_append_rows_not_aligned_for_bulk_copy(cuda, ref, lda):
     """Rows whose start is not 16-byte aligned (lda % 8 != 0) take the direct-load path; lda 2760 the
     bulk-copy one. Both bit-exact against the reference."""
     from glmkv import workload as W
@@ -282,5 +267,5 @@ def test_append_rows_not_aligned_for_bulk_copy(cuda, lda):
     wide[:, :case.x.shape[1]] = case.x
     wide[:, case.x.shape[1]:] = 0x7FC0  # padding columns: NaN if anything read them
     case.x, case.lda = wide, lda
-    got, ref = _run_both(case, cuda, full=True)
-    _assert_all_equal(got, ref, f"lda {lda}")
+    got, want = _run_both(case, cuda, full=True)
+    _assert_all_equal(got, want, f"lda {lda}")

@@ -33,14 +33,13 @@ def run_case(c, full, impl, cuda):
 
 @pytest.mark.parametrize("full", [True, False])
 @pytest.mark.parametrize("T", [1, 37, 512])
-def test_q_post_vs_reference_and_oracle(cuda, full, T):
-    from oracle import cpu, ref
+def test_q_post_vs_reference_and_oracle(cuda, ref, full, T):
+    from oracle import cpu
     c = q_post_case(T, 100 + T)
     got = run_case(c, full, "glmkv", cuda)
-    if ref.available():
-        want = run_case(c, full, "reference", cuda)
-        for g, w, name in zip(got, want, ("qmla", "iq", "wout")):
-            assert_equal(g, w, f"q_post vs reference: {name}")
+    want = run_case(c, full, "reference", cuda)
+    for g, w, name in zip(got, want, ("qmla", "iq", "wout")):
+        assert_equal(g, w, f"q_post vs reference: {name}")
     qmla = np.full(T * 64 * 576, 0x1234, np.uint16)
     iq = np.zeros(T * 32 * 128, np.uint8)
     wout = np.zeros(T * 32, np.float32)
@@ -51,21 +50,15 @@ def test_q_post_vs_reference_and_oracle(cuda, full, T):
 
 
 @pytest.mark.parametrize("full", [True, False])
-def test_q_post_16384_rows_vs_reference(cuda, full):
-    from oracle import ref
-    if not ref.available():
-        pytest.skip("reference library not built")
+def test_q_post_16384_rows_vs_reference(cuda, ref, full):
     c = q_post_case(16384, 7)
     for g, w, name in zip(run_case(c, full, "glmkv", cuda), run_case(c, full, "reference", cuda),
                           ("qmla", "iq", "wout")):
         assert_equal(g, w, f"16384 rows: {name}")
 
 
-def test_q_post_wider_rows(cuda):
+def test_q_post_wider_rows(cuda, ref):
     """qb rows wider than the 20,480 columns the op reads (ldb 20,488)."""
-    from oracle import ref
-    if not ref.available():
-        pytest.skip("reference library not built")
     c = q_post_case(64, 3, ldb=LDB + 8)
     for g, w, name in zip(run_case(c, True, "glmkv", cuda), run_case(c, True, "reference", cuda),
                           ("qmla", "iq", "wout")):
