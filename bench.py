@@ -53,6 +53,7 @@ def parse():
     ap.add_argument("--workload", choices=tuple(WORKLOADS), default="cfg3")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cfg2", action="store_true", help="skip the 1M-context (cfg2) layer block")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--no-next-rows", action="store_true",
@@ -197,30 +198,100 @@ def topk_picks(torch, call, group, gen, layers=None):
 
 # ------------------------------------------------------------------------------------------ the reference arm
 
-def run_call_reference(group, meta, inputs, ind, ctx, on_dequant=None):
-    """The same call through the reference's own kernels (oracle/_ref), manifest launch grids."""
+def run_call_reference(group, meta, inputs, ind, ctx, on_dequant=None, on_op=None):
+    """The same call through the reference's own kernels (oracle/_ref), manifest launch grids. The hooks
+    are LayerGroup.run_call's."""
     from glmkv.stage import FULL
     from oracle import ref
 
     p = lambda t: t.data_ptr()
+    hook = on_op or (lambda op, l, before: None)
     T, nseq, mp = meta.T, meta.nseq, meta.max_pages
+    hook("plan", None, True)
     ref.plan(p(meta.cu), p(meta.seq_lens), nseq, p(group.pos), p(group.ks), p(group.ke), p(group.klen),
              p(group.row_seq), p(group.zero), T)
+    hook("plan", None, False)
     for l in group.layers:
         a = inputs[l]
         full = l in FULL
+        hook("mla_prep", l, True)
         ref.mla_prep(True, p(a.x), a.x.shape[1], p(a.g_q), p(a.g_kv), p(group.rope), p(group.pos), p(meta.slot),
                      p(group.kv[l]), p(group.idx[l]) if full else None, p(a.ik_w) if full else None,
                      p(a.ik_b) if full else None, p(group.qq), p(group.qsf), group.sf_rows, T)
+        hook("mla_prep", l, False)
         if full:
+            hook("idx_gather", l, True)
             ref.idx_gather(p(group.idx[l]), p(meta.block_table), mp, p(meta.seq_lens), nseq, p(group.kg),
                            p(group.ksf), ctx)
+            hook("idx_gather", l, False)
+            hook("topk", l, True)
             ref.topk_stream(p(ind[l]), p(group.ks), p(group.klen), p(group.tlen), T)
+            hook("topk", l, False)
         if on_dequant:
             on_dequant(l, True)
+        hook("kv_dequant", l, True)
         ref.kv_dequant(p(group.kv[l]), p(meta.block_table), mp, p(meta.seq_lens), nseq, p(group.kvd), ctx)
+        hook("kv_dequant", l, False)
         if on_dequant:
             on_dequant(l, False)
+
+
+class OpTimer:
+    """CUDA events on the launch stream around every kernel of one target layer a step (and around the
+    stage's row plan every step): per-kernel device time inside the timed region."""
+    KERNELS = {"plan": "glm_plan", "mla_prep.indexer_layer": "glm_mla_prep_fp8",
+               "mla_prep.shared_layer": "glm_mla_prep_fp8", "idx_gather": "glm_idx_gather",
+               "topk": "glm_topk_stream", "kv_dequant": "glm_kv_dequant"}
+
+    def __init__(self, torch):
+        self.torch, self.target, self.open, self.spans = torch, None, {}, {}
+
+    @staticmethod
+    def key(op, l):
+        from glmkv.stage import FULL
+        if op == "mla_prep":
+            return "mla_prep.indexer_layer" if l in FULL else "mla_prep.shared_layer"
+        return op
+
+    def __call__(self, op, l, before):
+        if op != "plan" and l != self.target:
+            return
+        e = self.torch.cuda.Event(enable_timing=True)
+        e.record()
+        k = self.key(op, l)
+        if before:
+            self.open[k] = e
+        else:
+            self.spans.setdefault(k, []).append((self.open.pop(k), e))
+
+    def mean_us(self, k):
+        sp = self.spans.get(k, [])
+        return sum(a.elapsed_time(b) for a, b in sp) / len(sp) * 1e3 if sp else None
+
+    def per_op(self, call, peak):
+        """{op: kernel, launches timed, mean us, algorithmic bytes a launch, GB/s, fraction of `peak`}."""
+        from glmkv import traffic
+
+        nbytes = {"plan": traffic.plan(call.T, call.nseq), "mla_prep.indexer_layer": traffic.mla_prep(call.T, True),
+                  "mla_prep.shared_layer": traffic.mla_prep(call.T, False), "idx_gather": traffic.idx_gather(call.ctx),
+                  "topk": traffic.topk(call.T), "kv_dequant": traffic.kv_dequant(call.ctx)}
+        out = {}
+        for k, b in nbytes.items():
+            us = self.mean_us(k)
+            if us is None:
+                continue
+            gbs = b / us / 1e3
+            out[k] = {"kernel": self.KERNELS[k], "launches_timed": len(self.spans[k]), "us": round(us, 2),
+                      "algorithmic_bytes": b, "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4)}
+        us = self.mean_us("mla_prep.shared_layer")
+        if us is not None:
+            b = 1808 * call.T
+            out["kv_append_slice"] = {
+                "bytes_per_fresh_row": 1808, "algorithmic_bytes": b, "us": round(us, 2),
+                "GB/s": round(b / us / 1e3, 1), "frac": round(b / us / 1e3 / peak, 4),
+                "note": "the latent-row slice of the append alone (kv_a + k_pe read, the 656-byte fp8 row "
+                        "written) over the whole append kernel's time on a shared layer, which also quantizes q"}
+        return out
 
 
 # ------------------------------------------------------------------------------------------ next rows
@@ -426,6 +497,121 @@ def mqa_row(torch, impl, group, meta, call, dev, reps=3, sub=1024):
                          "peak_note": f"dense e4m3 = 2 x the {kind} bf16 GEMM rate (MEASURED_PEAKS.json bf16_tflops)"}}
 
 
+def isolated_ops(torch, impl, group, meta, inputs, ind, call, peak, passes=2):
+    """Each kernel of the path launched back to back over the stage's layers (each launch on its own
+    layer's inputs and cache state, all larger than L2), `passes` times, after one untimed pass: the
+    kernel's own rate, with the write-back of the launch before it being the same kernel's. Events
+    bracket each run of launches."""
+    from glmkv import ops, traffic
+    from glmkv.stage import FULL
+
+    T, nseq, mp = call.T, call.nseq, meta.max_pages
+    full = [l for l in group.layers if l in FULL]
+    shared = [l for l in group.layers if l not in FULL]
+    pp = lambda t: t.data_ptr()
+    if impl == "glmkv":
+        def prep(l):
+            a = inputs[l]
+            if l in FULL:
+                ops.mla_prep_full(a.x, a.x.shape[1], a.g_q, a.g_kv, group.rope, group.pos, meta.slot, group.kv[l],
+                                  group.idx[l], a.ik_w, a.ik_b, group.qq, group.qsf, group.sf_rows, T)
+            else:
+                ops.mla_prep_shared(a.x, a.x.shape[1], a.g_q, a.g_kv, group.rope, group.pos, meta.slot, group.kv[l],
+                                    group.qq, group.qsf, group.sf_rows, T)
+        gather = lambda l: ops.idx_gather(group.idx[l], meta.block_table, mp, meta.seq_lens, nseq, group.kg, group.ksf)
+        topk = lambda l: ops.topk_stream(ind[l], group.ks, group.klen, group.tlen, T)
+        dequant = lambda l: ops.kv_dequant(group.kv[l], meta.block_table, mp, meta.seq_lens, nseq, group.kvd)
+    else:
+        from oracle import ref
+
+        def prep(l):
+            a = inputs[l]
+            f = l in FULL
+            ref.mla_prep(True, pp(a.x), a.x.shape[1], pp(a.g_q), pp(a.g_kv), pp(group.rope), pp(group.pos),
+                         pp(meta.slot), pp(group.kv[l]), pp(group.idx[l]) if f else None, pp(a.ik_w) if f else None,
+                         pp(a.ik_b) if f else None, pp(group.qq), pp(group.qsf), group.sf_rows, T)
+        gather = lambda l: ref.idx_gather(pp(group.idx[l]), pp(meta.block_table), mp, pp(meta.seq_lens), nseq,
+                                          pp(group.kg), pp(group.ksf), call.ctx)
+        topk = lambda l: ref.topk_stream(pp(ind[l]), pp(group.ks), pp(group.klen), pp(group.tlen), T)
+        dequant = lambda l: ref.kv_dequant(pp(group.kv[l]), pp(meta.block_table), mp, pp(meta.seq_lens), nseq,
+                                           pp(group.kvd), call.ctx)
+    runs = [("mla_prep.indexer_layer", "glm_mla_prep_fp8", prep, full, traffic.mla_prep(T, True)),
+            ("mla_prep.shared_layer", "glm_mla_prep_fp8", prep, shared, traffic.mla_prep(T, False)),
+            ("idx_gather", "glm_idx_gather", gather, full, traffic.idx_gather(call.ctx)),
+            ("topk", "glm_topk_stream", topk, full, traffic.topk(T)),
+            ("kv_dequant", "glm_kv_dequant", dequant, group.layers, traffic.kv_dequant(call.ctx))]
+    out = {}
+    for name, kernel, fn, layers, nbytes in runs:
+        if not layers:
+            continue
+        for l in layers:
+            fn(l)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(passes):
+            for l in layers:
+                fn(l)
+        e.record()
+        torch.cuda.synchronize()
+        n = passes * len(layers)
+        us = s.elapsed_time(e) / n * 1e3
+        gbs = nbytes / us / 1e3
+        out[name] = {"kernel": kernel, "launches": n, "us": round(us, 2), "algorithmic_bytes": nbytes,
+                     "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4)}
+    if "mla_prep.shared_layer" in out:
+        us = out["mla_prep.shared_layer"]["us"]
+        b = 1808 * T
+        out["kv_append_slice"] = {"bytes_per_fresh_row": 1808, "algorithmic_bytes": b, "us": us,
+                                  "GB/s": round(b / us / 1e3, 1), "frac": round(b / us / 1e3 / peak, 4)}
+    return out
+
+
+# ------------------------------------------------------------------------------------------ the 1M-context call
+
+def cfg2_block(torch, impl, dev, seed, peak, steps=20, warmup=3):
+    """cfg2 (one sequence of 2^20 stream tokens, 16,384 fresh rows) through one indexer layer: the
+    whole layer's GB/s over `steps` timed steps, then each kernel's time in `steps` more steps with
+    events around every launch."""
+    from glmkv import stage, traffic, workload as W
+
+    call = W.config("cfg2", seed=seed)
+    group = stage.LayerGroup(0, 1, n_pages=call.n_pages, max_ctx=call.ctx, chunk=call.T, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(777 + seed)
+    group.rope = torch.from_numpy(W.rope_table(int(call.seq_lens.max())).view(np.int16)).to(dev).view(torch.bfloat16)
+    fill_caches(torch, group, gen)
+    inputs = layer_inputs(torch, group, call.T, gen)
+    ind = topk_picks(torch, call, group, gen)
+    meta = device_call(torch, call, dev)
+    if impl == "glmkv":
+        run = lambda hook=None: group.run_call(meta, inputs, ind, on_op=hook)
+    else:
+        run = lambda hook=None: run_call_reference(group, meta, inputs, ind, call.ctx, on_op=hook)
+    for _ in range(warmup):
+        run()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(steps):
+        run()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    timer = OpTimer(torch)
+    timer.target = 0
+    for _ in range(steps):
+        run(timer)
+    torch.cuda.synchronize()
+    nbytes = traffic.plan(call.T, call.nseq) + stage.layer_bytes(0, call.T, call.ctx)
+    out = {"workload": WORKLOADS["cfg2"], "seed": seed, "stream_tokens": call.ctx, "fresh_rows": call.T,
+           "steps": steps, "ms_per_step": round(ms, 4), "algorithmic_bytes_per_step": nbytes,
+           "value": round(nbytes / ms / 1e6, 1), "unit": "GB/s", "frac": round(nbytes / ms / 1e6 / peak, 4),
+           "per_op": timer.per_op(call, peak)}
+    del group, inputs, ind, meta
+    torch.cuda.empty_cache()
+    return out
+
+
 # ------------------------------------------------------------------------------------------ CPU baseline
 
 def cpu_baseline(call, layers, budget_s, seed):
@@ -499,9 +685,9 @@ def main():
     torch.cuda.synchronize()
 
     if a.impl == "glmkv":
-        run = lambda hook=None: group.run_call(meta, inputs, ind, on_dequant=hook)
+        run = lambda hook=None: group.run_call(meta, inputs, ind, on_op=hook)
     else:
-        run = lambda hook=None: run_call_reference(group, meta, inputs, ind, call.ctx, on_dequant=hook)
+        run = lambda hook=None: run_call_reference(group, meta, inputs, ind, call.ctx, on_op=hook)
     launches_per_step = group.launches_per_call()
 
     barrier = gd.barrier
@@ -514,16 +700,10 @@ def main():
         run()
     torch.cuda.synchronize()
     barrier()
-    # per-kernel timing inside the timed region: one dequant launch a step (a different layer each
-    # step), bracketed by two events on the launch stream
-    ev, target = [], [None]
+    # per-kernel timing inside the timed region: events around every kernel of one layer a step (a
+    # different layer each step) and around the stage's row plan, on the launch stream
+    timer = OpTimer(torch)
     layers = group.layers
-
-    def hook(l, before):
-        if l == target[0]:
-            e = torch.cuda.Event(enable_timing=True)
-            e.record()
-            ev.append(e)
 
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(ids, enabled=(rank == 0 and not a.no_clocks)) as clk:
@@ -531,15 +711,15 @@ def main():
         barrier()
         start.record()
         for i in range(a.steps):
-            target[0] = layers[i % len(layers)]
-            run(hook)
+            timer.target = layers[i % len(layers)]
+            run(timer)
         end.record()
         torch.cuda.synchronize()
         barrier()
     ms = start.elapsed_time(end)
     ms_max = max_over_ranks(ms)
-    dq_ms = sum(ev[i].elapsed_time(ev[i + 1]) for i in range(0, len(ev), 2))
-    dq_launches = len(ev) // 2
+    dq_us = timer.mean_us("kv_dequant")
+    dq_launches = len(timer.spans.get("kv_dequant", []))
 
     # ---- end to end through the public API: metadata from pinned host memory in, tlen out
     e2e = None
@@ -581,17 +761,17 @@ def main():
     value = total_bytes / step_s / 1e9
     peak, peak_kind = measured_peak()
     dq_bytes = traffic.kv_dequant(call.ctx)
-    dq_avg_s = dq_ms / max(dq_launches, 1) / 1e3
+    dq_avg_s = (dq_us or 0.0) / 1e6
     achieved = dq_bytes / dq_avg_s / 1e9 if dq_launches else None
     launches_total = int(gd.sum_over_ranks(launches_per_step * a.steps, device=dev))
 
     traffic_rec = None
     tp = ROOT / "profiles" / "ncu_traffic.json"
-    if tp.exists():
+    if tp.exists() and a.impl == "glmkv":
         try:
             rec = json.loads(tp.read_text()).get("glm_kv_dequant")
             if rec:
-                traffic_rec = rec["dram_bytes_per_stream_token"] * call.ctx
+                traffic_rec = round(rec["dram_bytes_per_stream_token"] * call.ctx)
         except (ValueError, KeyError):
             traffic_rec = None
 
@@ -632,11 +812,23 @@ def main():
         "ideal_speedup_vs_1gpu": round(ideal, 3),
         "roofline": {"kernel": "glm_kv_dequant", "bound": "hbm", "achieved": round(achieved, 1) if achieved else None,
                      "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None,
-                     "traffic": traffic_rec, "algorithmic_bytes_per_launch": dq_bytes,
+                     "traffic": traffic_rec,
+                     "traffic_source": "recorded, not captured in this run: ncu dram__bytes_read.sum + "
+                                       "dram__bytes_write.sum of one full-size launch (profiles/ncu_traffic.json), "
+                                       "per stream token, times this call's stream tokens" if traffic_rec else None,
+                     "algorithmic_bytes_per_launch": dq_bytes,
                      "avg_launch_us": round(dq_avg_s * 1e6, 2), "launches_timed": dq_launches,
                      "peak_note": f"{peak_kind} HBM copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"},
         "gpu_launches": launches_total,
         "clocks": clk.summary(),
+        "per_op": {
+            "note": f"algorithmic bytes per launch over CUDA-event time, fraction of the {peak_kind} HBM peak. "
+                    "in_step: events around every kernel of one layer a step inside the timed steps (these "
+                    "launches lose the PDL overlap with their neighbours and pay the write-back of the previous "
+                    "kernel's dirty L2 lines); isolated: each kernel back to back over the stage's layers after "
+                    "the timed steps",
+            "in_step": timer.per_op(call, peak),
+            "isolated": isolated_ops(torch, a.impl, group, meta, inputs, ind, call, peak)},
     }
     if e2e is not None:
         e2e_ms, h2d, d2h, wall = e2e
@@ -648,6 +840,8 @@ def main():
                                "seq_lens, block_table, slot_mapping copied from pinned host memory each step and "
                                "tlen read back" if a.impl == "glmkv" else
                                "reference kernels (oracle/_ref) with the same host copies"}
+    if world == 1 and a.workload == "cfg3" and not a.no_cfg2:
+        line["cfg2"] = cfg2_block(torch, a.impl, dev, a.seed, peak)
     if not a.no_next_rows:
         line["next_rows"] = next_rows(torch, a.impl, call.T, dev)
         line["next_rows"]["glm_mqa_logits_paged"] = mqa_row(torch, a.impl, group, meta, call, dev)

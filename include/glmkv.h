@@ -8,6 +8,12 @@
  * different streams. The same kernels, with the same entry names and parameter lists, are also built
  * as the cubin `glm_glue_b200.cubin` for a kern manifest.
  *
+ * Launches use programmatic dependent launch (unless the environment sets GLMKV_PDL=0): a kernel may
+ * start while the kernel before it on the stream drains, and waits for it before it reads anything
+ * that kernel can have written. The one exception is the append's norm weights (g_q, g_kv, ik_w,
+ * ik_b), load-time constants read before that wait: they must not be written by the kernel launched
+ * just before the append.
+ *
  * Return value: GLMKV_OK, or a GLMKV_ERR_* code when an argument is invalid (nothing is launched) or
  * the launch failed. Device-side conditions (an invalid page number in a block table, a bounded wait
  * that gave up) are recorded in the module's fault word, read with glmkv_fault_flags().

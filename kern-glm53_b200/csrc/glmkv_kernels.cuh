@@ -366,23 +366,11 @@ __device__ __forceinline__ void prep_rows(const bf16* __restrict__ x, int lda, c
     mbar_init_fence();
   }
   pdl_trigger();  // a persistent grid: all of its CTAs are resident
-  pdl_wait();
-
-  const int stride = gridDim.x * PREP_WARPS;
-  int r = blockIdx.x * PREP_WARPS + warp;
-  const bool bulk = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (lda & 7) == 0;
-  const uint32_t bytes = idx != nullptr ? PREP_ROW : 2 * (QL + MLA);
-  u8* buf = smem + PREP_WGT + (size_t)warp * PREP_BUFS * PREP_ROW;
-  auto issue = [&](int b, int row) {
-    const uint32_t mb = smem_u32(&bar[warp][b]);
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_arrive_expect_tx(mb, bytes);
-    tma_load_1d(smem_u32(buf + b * PREP_ROW), x + (size_t)row * lda, bytes, mb);
-  };
-  if (bulk && r < T && l == 0) issue(0, r);  // the warp's first row is on its way while the weights are staged
 
   // The norm weights as f32, every load in flight at once (g_q and the indexer weights 8-byte aligned,
-  // g_kv 4-byte aligned; the launcher checks).
+  // g_kv 4-byte aligned; the launcher checks). They are load-time weights that no kernel of the path
+  // writes, so they are staged before the wait for the previous kernel on the stream: under
+  // programmatic dependent launch this overlaps that kernel's tail.
   {
     const uint2 q0 = __ldg(reinterpret_cast<const uint2*>(g_q) + tid);
     const uint2 q1 = __ldg(reinterpret_cast<const uint2*>(g_q) + PREP_THREADS + tid);
@@ -399,6 +387,20 @@ __device__ __forceinline__ void prep_rows(const bf16* __restrict__ x, int lda, c
       *reinterpret_cast<float4*>((tid < ID / 4 ? wik : wib) + 4 * (tid & (ID / 4 - 1))) =
           make_float4(bf_lo(w.x), bf_hi(w.x), bf_lo(w.y), bf_hi(w.y));
   }
+  pdl_wait();  // x, pos and slot come from the kernels before this one
+
+  const int stride = gridDim.x * PREP_WARPS;
+  int r = blockIdx.x * PREP_WARPS + warp;
+  const bool bulk = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (lda & 7) == 0;
+  const uint32_t bytes = idx != nullptr ? PREP_ROW : 2 * (QL + MLA);
+  u8* buf = smem + PREP_WGT + (size_t)warp * PREP_BUFS * PREP_ROW;
+  auto issue = [&](int b, int row) {
+    const uint32_t mb = smem_u32(&bar[warp][b]);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_arrive_expect_tx(mb, bytes);
+    tma_load_1d(smem_u32(buf + b * PREP_ROW), x + (size_t)row * lda, bytes, mb);
+  };
+  if (bulk && r < T && l == 0) issue(0, r);
   __syncthreads();
 
   if (r >= T) return;

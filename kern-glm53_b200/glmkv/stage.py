@@ -135,32 +135,46 @@ class LayerGroup:
     def bytes_per_call(self, T, ctx, nseq):
         return traffic.plan(T, nseq) + sum(layer_bytes(l, T, ctx, self.kv_dtype) for l in self.layers)
 
-    def run_call(self, meta: CallMeta, inputs, ind, stream=None, on_dequant=None):
+    def run_call(self, meta: CallMeta, inputs, ind, stream=None, on_dequant=None, on_op=None):
         """The cache path of one call through the group's layers. `inputs[l]` is a LayerInputs,
         `ind[l]` the top-k picks [T, 2048] i32 of indexer layer l (rewritten in place).
-        `on_dequant(l, before)` is called around each dequant launch (for per-kernel timing)."""
+        `on_op(op, l, before)` is called around every launch (op one of "plan", "mla_prep",
+        "idx_gather", "topk", "kv_dequant"; l None for the stage's plan), and `on_dequant(l, before)`
+        around each dequant launch: hooks for per-kernel timing."""
         T, nseq, mp = meta.T, meta.nseq, meta.max_pages
+        hook = on_op or (lambda op, l, before: None)
+        hook("plan", None, True)
         ops.plan(meta.cu, meta.seq_lens, nseq, self.pos, self.ks, self.ke, self.klen, self.row_seq, self.zero, T,
                  stream=stream)
+        hook("plan", None, False)
         for l in self.layers:
             a = inputs[l]
+            hook("mla_prep", l, True)
             if l in FULL:
                 ops.mla_prep_full(a.x, a.x.shape[1], a.g_q, a.g_kv, self.rope, self.pos, meta.slot, self.kv[l],
                                   self.idx[l], a.ik_w, a.ik_b, self.qq, self.qsf, self.sf_rows, T,
                                   kv_dtype=self.kv_dtype, stream=stream)
+                hook("mla_prep", l, False)
+                hook("idx_gather", l, True)
                 ops.idx_gather(self.idx[l], meta.block_table, mp, meta.seq_lens, nseq, self.kg, self.ksf,
                                stream=stream)
+                hook("idx_gather", l, False)
+                hook("topk", l, True)
                 if self.kv_dtype == "fp8":
                     ops.topk_stream(ind[l], self.ks, self.klen, self.tlen, T, stream=stream)
                 else:
                     ops.topk_slots(ind[l], meta.block_table, mp, self.row_seq, self.klen, self.tlen, T, stream=stream)
+                hook("topk", l, False)
             else:
                 ops.mla_prep_shared(a.x, a.x.shape[1], a.g_q, a.g_kv, self.rope, self.pos, meta.slot, self.kv[l],
                                     self.qq, self.qsf, self.sf_rows, T, kv_dtype=self.kv_dtype, stream=stream)
+                hook("mla_prep", l, False)
             if self.kv_dtype == "fp8":
                 if on_dequant:
                     on_dequant(l, True)
+                hook("kv_dequant", l, True)
                 ops.kv_dequant(self.kv[l], meta.block_table, mp, meta.seq_lens, nseq, self.kvd, stream=stream)
+                hook("kv_dequant", l, False)
                 if on_dequant:
                     on_dequant(l, False)
         self.launches += self.launches_per_call()
