@@ -54,6 +54,10 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cfg2", action="store_true", help="skip the 1M-context (cfg2) layer block")
+    ap.add_argument("--cuts", default=None, help="first layers of the stages, comma-separated (overrides --placement)")
+    ap.add_argument("--placement", choices=("any", "indexer"), default="any",
+                    help="stage cuts at any layer, with the picks forwarded to a stage that starts at a shared "
+                         "layer (default), or at indexer layers only (the reference's deployment rule)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--no-next-rows", action="store_true",
@@ -234,6 +238,16 @@ def run_call_reference(group, meta, inputs, ind, ctx, on_dequant=None, on_op=Non
         hook("kv_dequant", l, False)
         if on_dequant:
             on_dequant(l, False)
+
+
+def compose(*hooks):
+    """One on_op hook that calls each of `hooks` (None entries skipped) in order."""
+    hs = [h for h in hooks if h is not None]
+    if not hs:
+        return None
+    if len(hs) == 1:
+        return hs[0]
+    return lambda op, l, before: [h(op, l, before) for h in hs] and None
 
 
 class OpTimer:
@@ -657,16 +671,27 @@ def main():
     world, rank, local = gd.env()
     if world != a.gpus:
         raise SystemExit(f"--gpus {a.gpus} but WORLD_SIZE {world}")
+
+    call = W.config(a.workload, seed=a.seed)
+    any_layer = a.placement == "any"
+    if a.workload == "cfg3":
+        if a.cuts:
+            cuts = [int(x) for x in a.cuts.split(",")]
+            if len(cuts) != world or cuts[0] != 0 or cuts != sorted(set(cuts)) or cuts[-1] >= stage.LAYERS:
+                raise SystemExit(f"--cuts {a.cuts}: {world} increasing first layers from 0 below {stage.LAYERS}")
+        else:
+            cuts = list(stage.cuts(world, T=call.T, ctx=call.ctx, any_layer=any_layer))
+        first, last = (cuts + [stage.LAYERS])[rank], (cuts + [stage.LAYERS])[rank + 1]
+    else:  # single-layer workloads: every rank runs layer 0 (an indexer layer) of its own call
+        first, last, cuts = 0, 1, [0]
+    forwards = stage.forwarded_picks(cuts) if a.workload == "cfg3" else []
+    if forwards:  # before NCCL and the kernels start: p2p kernels on few SMs, and those SMs left to them
+        os.environ.setdefault("NCCL_MAX_P2P_NCHANNELS", str(stage.FORWARD_RESERVED_SMS))
+        if any(rank in (s_, r_) for s_, r_, _ in forwards):
+            os.environ.setdefault("GLMKV_RESERVE_SMS", str(stage.FORWARD_RESERVED_SMS))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     gd.init("nccl", timeout_s=300, device=dev)
-
-    call = W.config(a.workload, seed=a.seed)
-    if a.workload == "cfg3":
-        first, last = stage.group_of(rank, world, T=call.T, ctx=call.ctx)
-        cuts = list(stage.cuts(world, T=call.T, ctx=call.ctx))
-    else:  # single-layer workloads: every rank runs layer 0 (an indexer layer) of its own call
-        first, last, cuts = 0, 1, [0]
     if a.impl == "reference":
         from oracle import ref
         if not ref.available():
@@ -684,10 +709,17 @@ def main():
     meta = device_call(torch, call, dev)
     torch.cuda.synchronize()
 
+    # the picks of an indexer layer before a cut at a shared layer travel to the next stage every call
+    fwd = gd.PicksForwarder(cuts if a.workload == "cfg3" else [0], rank, call.T, dev, ind=ind, tlen=group.tlen)
     if a.impl == "glmkv":
-        run = lambda hook=None: group.run_call(meta, inputs, ind, on_op=hook)
+        call_path = lambda hook: group.run_call(meta, inputs, ind, on_op=hook)
     else:
-        run = lambda hook=None: run_call_reference(group, meta, inputs, ind, call.ctx, on_op=hook)
+        call_path = lambda hook: run_call_reference(group, meta, inputs, ind, call.ctx, on_op=hook)
+
+    def run(hook=None):
+        fwd.begin_call()
+        call_path(compose(fwd.hook if fwd.active else None, hook))
+        fwd.end_call()
     launches_per_step = group.launches_per_call()
 
     barrier = gd.barrier
@@ -698,6 +730,7 @@ def main():
     # ---- device-resident timing
     for _ in range(a.warmup):
         run()
+    fwd.drain()
     torch.cuda.synchronize()
     barrier()
     # per-kernel timing inside the timed region: events around every kernel of one layer a step (a
@@ -713,11 +746,13 @@ def main():
         for i in range(a.steps):
             timer.target = layers[i % len(layers)]
             run(timer)
+        fwd.drain()
         end.record()
         torch.cuda.synchronize()
         barrier()
     ms = start.elapsed_time(end)
     ms_max = max_over_ranks(ms)
+    rank_ms = gd.gather_objects(round(ms / a.steps, 4))
     dq_us = timer.mean_us("kv_dequant")
     dq_launches = len(timer.spans.get("kv_dequant", []))
 
@@ -737,6 +772,7 @@ def main():
 
         for _ in range(max(1, a.warmup // 2)):
             e2e_step()
+        fwd.drain()
         torch.cuda.synchronize()
         barrier()
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -744,6 +780,7 @@ def main():
         s2.record()
         for _ in range(a.steps):
             e2e_step()
+        fwd.drain()
         e2.record()
         torch.cuda.synchronize()
         wall = (time.perf_counter() - t0) * 1e3
@@ -792,6 +829,7 @@ def main():
         "steps": a.steps,
         "warmup": a.warmup,
         "ms_per_step": round(ms_max / a.steps, 4),
+        "rank_ms_per_step": rank_ms,
         "higher_is_better": True,
         "scaling": "strong" if a.workload == "cfg3" else "weak",
         "vs_baseline": None,
@@ -802,7 +840,15 @@ def main():
             "workload": WORKLOADS[a.workload], "seed": a.seed, "fresh_rows": call.T, "seqs": call.nseq,
             "stream_tokens": call.ctx, "kv_cache": "fp8_ds_mla (656 B/token) + indexer 132 B/token",
             "layers": (stage.LAYERS if a.workload == "cfg3" else world), "stage_cuts": cuts,
-            "parallelism": f"layer groups x{world} (pipeline stages at indexer layers), no collective",
+            "placement": ("cuts at indexer layers only" if not forwards else
+                          "cuts at any layer; the picks of the indexer layer before each cut at a shared layer "
+                          "are forwarded to the next stage every call (NCCL send/recv on a side stream)"),
+            "forwarded_picks": [{"from_rank": s_, "to_rank": r_, "indexer_layer": l_,
+                                 "bytes_per_call": stage.picks_bytes(call.T)} for s_, r_, l_ in forwards],
+            "reserved_sms_on_forwarding_ranks": stage.FORWARD_RESERVED_SMS if forwards else 0,
+            "parallelism": f"layer groups x{world} (pipeline stages)" + (
+                f", {len(forwards)} forward(s) of the picks a call by NCCL send/recv" if forwards else
+                ", no collective on the data path"),
             "l2": "no flush: every layer's cache pool and stream exceed the 126 MB L2",
             "storage": "e4m3 codes + f32 scales in, bf16 out; f32 arithmetic",
         },

@@ -26,7 +26,7 @@ constexpr size_t GA_SMEM = (size_t)GA_STAGES * IDX_PAGE;
 
 struct DeviceInfo {
   int status = GLMKV_OK;
-  int sms = 0;
+  int sms = 0;        // SMs the persistent grids are sized for: the device's, less GLMKV_RESERVE_SMS
   int dq_ctas = 0;    // resident dequant CTAs an SM
   int ga_ctas = 0;    // resident gather CTAs an SM
   int prep_ctas = 0;  // resident append CTAs an SM
@@ -47,6 +47,13 @@ const DeviceInfo* device_info() {
   std::call_once(g_once[dev], [dev] {
     DeviceInfo& d = g_info[dev];
     bool ok = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess;
+    // SMs left to other work that runs beside the path on the same GPU, such as a transfer kernel that
+    // stays resident while it waits for its peer: a persistent grid sized for every SM would otherwise
+    // have a CTA wait for that kernel, and the whole launch with it
+    if (const char* r = getenv("GLMKV_RESERVE_SMS")) {
+      const int reserve = atoi(r);
+      if (reserve > 0) d.sms = std::max(1, d.sms - reserve);
+    }
     ok = ok && cudaFuncSetAttribute(glm_kv_dequant, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DQ_SMEM) ==
                    cudaSuccess;
     ok = ok && cudaFuncSetAttribute(glm_idx_gather, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GA_SMEM) ==

@@ -28,9 +28,21 @@ def layer_bytes(l, T, ctx, kv_dtype="fp8"):
     return traffic.layer(T, ctx, l in FULL, kv_dtype)
 
 
-def cuts(n_groups, T=16384, ctx=1 << 20, kv_dtype="fp8"):
-    """First layers of `n_groups` stages, each at an indexer layer, minimising the largest stage's bytes."""
-    starts = sorted(FULL)
+# SMs a stage that sends or receives forwarded picks leaves to the transfer's kernels (NCCL's p2p
+# kernels stay resident while they wait for the peer), and the slowdown of such a stage's persistent
+# kernels that this costs, as measured on B200 (148 SMs): 4 SMs, about 3%
+FORWARD_RESERVED_SMS = 4
+FORWARD_SLOWDOWN = 0.03
+
+
+def cuts(n_groups, T=16384, ctx=1 << 20, kv_dtype="fp8", any_layer=False):
+    """First layers of `n_groups` stages, minimising the largest stage's cost. Each stage starts at an
+    indexer layer (the reference's rule, scripts/gen.py:491), or with `any_layer` at any layer: a stage
+    that then starts at a shared layer needs the picks of the indexer layer before it from the stage
+    that owns that layer (`forwarded_picks`). A stage's cost is its layers' algorithmic bytes; a stage
+    that sends or receives picks also pays the forwarded bytes and FORWARD_SLOWDOWN, so the solver cuts
+    at a shared layer only where the better balance outweighs the exchange."""
+    starts = list(range(LAYERS)) if any_layer else sorted(FULL)
     if n_groups < 1 or n_groups > len(starts):
         raise ValueError(f"{n_groups} stages: between 1 and {len(starts)}")
     w = [layer_bytes(l, T, ctx, kv_dtype) for l in range(LAYERS)]
@@ -40,6 +52,12 @@ def cuts(n_groups, T=16384, ctx=1 << 20, kv_dtype="fp8"):
     cand = starts + [LAYERS]
     end = len(cand) - 1
     INF = float("inf")
+    def stage_cost(a, b):  # layers [a, b): receives picks when a is a shared layer, sends when b is
+        c = pre[b] - pre[a]
+        recv, send = a not in FULL, b < LAYERS and b not in FULL
+        if recv or send:
+            c = c * (1 + FORWARD_SLOWDOWN) + picks_bytes(T) * (recv + send)
+        return c
 
     def solve(combine, limit):
         # best[k][i]: the objective for layers [cand[i], 78) in k stages, no stage above `limit`
@@ -49,7 +67,7 @@ def cuts(n_groups, T=16384, ctx=1 << 20, kv_dtype="fp8"):
         for k in range(1, n_groups + 1):
             for i in range(end):
                 for j in range(i + 1, len(cand)):
-                    c = pre[cand[j]] - pre[cand[i]]
+                    c = stage_cost(cand[i], cand[j])
                     if best[k - 1][j] == INF or c > limit:
                         continue
                     v = combine(c, best[k - 1][j])
@@ -69,9 +87,34 @@ def cuts(n_groups, T=16384, ctx=1 << 20, kv_dtype="fp8"):
     return tuple(out)
 
 
+def picks_bytes(T):
+    """Bytes of one forward of a call's picks: ind [T, 2048] i32 and tlen [T] i32."""
+    return 4 * T * 2048 + 4 * T
+
+
 def group_of(rank, n_groups, **kw):
     c = cuts(n_groups, **kw) + (LAYERS,)
     return c[rank], c[rank + 1]
+
+
+def picks_source(l):
+    """The indexer layer whose top-k picks layer `l` attends with: `l` itself on an indexer layer, else
+    the last indexer layer before it (a shared layer reuses its picks, scripts/gen.py:388-400)."""
+    return max(f for f in FULL if f <= l)
+
+
+def forwarded_picks(cut_list):
+    """[(sender, receiver, source layer)]: for every stage that starts at a shared layer, the stage that
+    owns the indexer layer whose picks its first layers use. Empty when every stage starts at an
+    indexer layer. Sent per call: the picks [T, 2048] i32 after the row plan, and tlen [T] i32."""
+    c = list(cut_list) + [LAYERS]
+    owner = lambda l: max(i for i in range(len(c) - 1) if c[i] <= l)
+    out = []
+    for k in range(1, len(c) - 1):
+        if c[k] not in FULL:
+            src = picks_source(c[k])
+            out.append((owner(src), k, src))
+    return out
 
 
 @dataclass
