@@ -54,6 +54,7 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cfg2", action="store_true", help="skip the 1M-context (cfg2) layer block")
+    ap.add_argument("--no-marked", action="store_true", help="skip the row-selective lift block")
     ap.add_argument("--cuts", default=None, help="first layers of the stages, comma-separated (overrides --placement)")
     ap.add_argument("--placement", choices=("any", "indexer"), default="any",
                     help="stage cuts at any layer, with the picks forwarded to a stage that starts at a shared "
@@ -581,6 +582,86 @@ def isolated_ops(torch, impl, group, meta, inputs, ind, call, peak, passes=2):
     return out
 
 
+def marked_block(torch, impl, group, meta, call, dev, peak, passes=2):
+    """The row-selective lift (glm_mark_rows + glm_kv_dequant_marked) on the call's layers, for two
+    pick distributions: the benchmark's uniform picks, and each row's 2048 latest positions (a sliding
+    window). The mask is built once from an indexer layer's picks (after the row plan) and serves the
+    lift of every layer; the lift is timed back to back over the stage's layers like `isolated_ops`."""
+    import glmkv
+    from glmkv import traffic
+    from glmkv.stage import FULL
+
+    if impl != "glmkv":
+        return {"unavailable": "the reference lifts every row: it has no row-selective lift"}
+    full = [l for l in group.layers if l in FULL]
+    if not full:
+        return {"unavailable": "no indexer layer in this stage"}
+    T, ctx, mp = call.T, call.ctx, meta.max_pages
+    words = (ctx + 63) // 64
+    g = torch.Generator(device=dev).manual_seed(11)
+    klen = group.klen[:T].to(torch.int64)
+    ar = torch.arange(2048, device=dev)
+    dists = {"uniform": topk_picks(torch, call, group, g, full[:1])[full[0]],
+             "sliding_window": torch.where(ar[None, :] < klen[:, None], (klen[:, None] - 2048).clamp(min=0) + ar[None, :],
+                                           -1).to(torch.int32).contiguous()}
+    mask = torch.empty(words, dtype=torch.int64, device=dev)
+    s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn, n):
+        fn()
+        torch.cuda.synchronize()
+        s_.record()
+        for _ in range(n):
+            fn()
+        e_.record()
+        torch.cuda.synchronize()
+        return s_.elapsed_time(e_) / n * 1e3
+
+    out = {"note": "mask from one indexer layer's picks after the row plan; lift timed back to back over the "
+                   "stage's layers; the full lift (glm_kv_dequant) timed the same way beside it"}
+    lift_all = lambda: [glmkv.kv_dequant(group.kv[l], meta.block_table, mp, meta.seq_lens, call.nseq, group.kvd)
+                        for l in group.layers]
+    full_us = timed(lift_all, passes) / len(group.layers)
+    for name, picks in dists.items():
+        ind = picks.clone()
+        glmkv.topk_stream(ind, group.ks, group.klen, group.tlen, T)
+        mark = lambda: glmkv.mark_rows(ind, group.ks, group.ke, T, mask, words)
+        mark_us = timed(mark, 5)
+        mark()
+        lift = lambda: [glmkv.kv_dequant_marked(group.kv[l], meta.block_table, mp, meta.seq_lens, call.nseq, mask,
+                                                group.kvd) for l in group.layers]
+        lift_us = timed(lift, passes) / len(group.layers)
+        bits = np.unpackbits(mask.cpu().numpy().view(np.uint8), bitorder="little")[:ctx].astype(bool)
+        # rows read: per page, the span from its first to its last marked row (the whole page when 48
+        # or more of its rows are marked); rows written: the marked ones, and all rows of such a page
+        goff = np.concatenate([[0], np.cumsum(call.seq_lens)[:-1]])
+        read_rows = written = 0
+        for s0, ln in zip(goff, call.seq_lens):
+            for j in range(0, int(ln), 64):
+                page = bits[s0 + j:s0 + min(j + 64, ln)]
+                idx = np.flatnonzero(page)
+                if idx.size >= 48:
+                    read_rows += page.size
+                    written += page.size
+                elif idx.size:
+                    read_rows += int(idx[-1] - idx[0] + 1)
+                    written += idx.size
+        marked = int(bits.sum())
+        lift_bytes = 656 * read_rows + 1152 * written
+        mark_bytes = 8192 * T + 8 * words
+        out[name] = {"marked_fraction": round(marked / ctx, 4), "rows_marked": marked, "rows_read": read_rows,
+                     "rows_written": written,
+                     "mark_us": round(mark_us, 2), "mark_GB/s": round(mark_bytes / mark_us / 1e3, 1),
+                     "lift_us": round(lift_us, 2), "lift_algorithmic_bytes": lift_bytes,
+                     "lift_GB/s": round(lift_bytes / lift_us / 1e3, 1),
+                     "lift_frac": round(lift_bytes / lift_us / 1e3 / peak, 4),
+                     "full_lift_us": round(full_us, 2),
+                     "full_lift_bytes": traffic.kv_dequant(ctx),
+                     "speedup_vs_full_lift_incl_mark_every_4_layers": round(full_us / (lift_us + mark_us / 4), 3)}
+        del ind
+    return out
+
+
 # ------------------------------------------------------------------------------------------ the 1M-context call
 
 def cfg2_block(torch, impl, dev, seed, peak, steps=20, warmup=3):
@@ -886,6 +967,8 @@ def main():
                                "seq_lens, block_table, slot_mapping copied from pinned host memory each step and "
                                "tlen read back" if a.impl == "glmkv" else
                                "reference kernels (oracle/_ref) with the same host copies"}
+    if a.workload == "cfg3" and not a.no_marked:
+        line["marked_lift"] = marked_block(torch, a.impl, group, meta, call, dev, peak)
     if world == 1 and a.workload == "cfg3" and not a.no_cfg2:
         line["cfg2"] = cfg2_block(torch, a.impl, dev, a.seed, peak)
     if not a.no_next_rows:

@@ -89,6 +89,27 @@ int glmkv_idx_gather(const void* idx, const int32_t* block_table, int max_pages,
 int glmkv_kv_dequant(const void* kv, const int32_t* block_table, int max_pages, const int32_t* seq_lens, int nseq,
                      void* kvd, glmkv_stream_t stream);
 
+/* The stream rows a call's picks name, as a bitmap for glmkv_kv_dequant_marked: bit p % 64 of word
+ * p / 64 of mask is set for every pick p >= 0 of ind [T, 2048] i32 (stream rows: glmkv_topk_stream's
+ * output). ks and ke [T] u32 are glm_plan's: row r's picks lie in [ks[r], ke[r]). The launcher first
+ * clears mask [mask_words] (one memset on `stream`; mask_words >= ceil(stream rows / 64)). A pick at or
+ * past mask_words * 64 is skipped and sets fault bit 4. The shared layers after an indexer layer attend
+ * with its picks, so one mask serves them all. Needs ind 16-byte aligned, mask 8.
+ * No counterpart in the reference, which lifts every row (kern-glm53 source/glm_glue.cu:378-414). */
+int glmkv_mark_rows(const int32_t* ind, const uint32_t* ks, const uint32_t* ke, int T, uint64_t* mask, int mask_words,
+                    glmkv_stream_t stream);
+
+/* glmkv_kv_dequant restricted to the rows mask marks (glmkv_mark_rows): every marked stream row gets
+ * exactly the bytes glmkv_kv_dequant writes there. A page with no marked row is neither read nor
+ * written. A page with 48 or more marked rows is lifted whole (its other rows get the bytes
+ * glmkv_kv_dequant writes there); of the other pages only the span from the first to the last marked
+ * row is read and only the marked rows are written. mask holds ceil(stream rows / 64) words. Needs kv
+ * and kvd 16-byte aligned, mask 8.
+ * No counterpart in the reference (its op `kv_dequant`, kern-glm53 scripts/gen.py:133-135, lifts every
+ * row; FlashMLA reads only the picked rows, scripts/gen.py:399-400). */
+int glmkv_kv_dequant_marked(const void* kv, const int32_t* block_table, int max_pages, const int32_t* seq_lens,
+                            int nseq, const uint64_t* mask, void* kvd, glmkv_stream_t stream);
+
 /* Top-k picks [T, 2048] i32 (sequence-relative, -1 padded) -> stream rows, in place; tlen [T].
  * Replaces op `topk_stream` -> glm_topk_stream (kern-glm53 scripts/gen.py:130-132;
  * source/glm_glue.cu:419-428). Needs ind 16-byte aligned. */
@@ -143,7 +164,8 @@ int glmkv_mqa_logits_paged(const void* iq, const void* idx, int n_pages, const i
 
 /* The launch shape (grid x, block x, dynamic shared memory bytes) libglmkv uses for the kernel
  * `entry` ("glm_plan", "glm_mla_prep", "glm_mla_prep_fp8", "glm_idx_gather", "glm_kv_dequant",
- * "glm_topk_stream", "glm_topk_slots", "glm_q_post", "glm_add_rms_quant", "glm_mqa_logits_paged") on
+ * "glm_topk_stream", "glm_topk_slots", "glm_q_post", "glm_add_rms_quant", "glm_mqa_logits_paged",
+ * "glm_mark_rows", "glm_kv_dequant_marked") on
  * the current device for a call of T fresh rows: what a kern
  * manifest's `impl.launches` entry for the cubin must use. The persistent page kernels depend on the
  * device's SM count only. No counterpart in the reference, whose shapes are fixed in its manifest
@@ -157,7 +179,7 @@ int glmkv_launch_shape(const char* entry, int T, int* grid, int* block, int* sme
 int glmkv_selftest_wait(uint64_t limit_ns, uint32_t* waited_ns, glmkv_stream_t stream);
 
 /* Device-side fault bits of the current device's module (1: a bounded wait gave up; 2: a block
- * table named a negative page, which was skipped). Synchronises the device; clears the word when
+ * table named a negative page, which was skipped; 4: a pick past the mark bitmap, skipped). Synchronises the device; clears the word when
  * `clear` is non-zero. No counterpart in the reference, whose kernels report nothing. */
 int glmkv_fault_flags(uint32_t* flags, int clear);
 

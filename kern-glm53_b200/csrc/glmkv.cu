@@ -60,6 +60,10 @@ const DeviceInfo* device_info() {
                    cudaSuccess;
     ok = ok && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.dq_ctas, glm_kv_dequant, DQ_THREADS, DQ_SMEM) ==
                    cudaSuccess;
+    ok = ok && cudaFuncSetAttribute(glm_kv_dequant_marked, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)DQ_SMEM) == cudaSuccess;
+    ok = ok && cudaFuncSetAttribute(glm_mark_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, MK_SMEM) ==
+                   cudaSuccess;
     ok = ok && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.ga_ctas, glm_idx_gather, GA_THREADS, GA_SMEM) ==
                    cudaSuccess;
     for (auto k : {glm_mla_prep, glm_mla_prep_fp8})
@@ -197,6 +201,38 @@ GLMKV_API int glmkv_kv_dequant(const void* kv, const int32_t* block_table, int m
                 max_pages, seq_lens, nseq, (bf16*)kvd);
 }
 
+GLMKV_API int glmkv_mark_rows(const int32_t* ind, const uint32_t* ks, const uint32_t* ke, int T, uint64_t* mask,
+                              int mask_words, glmkv_stream_t stream) {
+  if (T < 0 || mask_words < 0) return GLMKV_ERR_ARG;
+  if (mask_words == 0) return T == 0 ? GLMKV_OK : GLMKV_ERR_ARG;
+  if (!mask) return GLMKV_ERR_ARG;
+  if (!aligned(mask, 8)) return GLMKV_ERR_ALIGN;
+  if (T > 0 && (!ind || !ks || !ke)) return GLMKV_ERR_ARG;
+  if (T > 0 && !aligned(ind, 16)) return GLMKV_ERR_ALIGN;
+  const DeviceInfo* d = device_info();
+  if (!d) return GLMKV_ERR_DEVICE;
+  if (cudaMemsetAsync(mask, 0, (size_t)mask_words * 8, (cudaStream_t)stream) != cudaSuccess) {
+    cudaGetLastError();
+    return GLMKV_ERR_LAUNCH;
+  }
+  if (T == 0) return GLMKV_OK;
+  return launch(glm_mark_rows, std::min(d->sms, (T + MK_RB - 1) / MK_RB), MK_THREADS, MK_SMEM, stream, (const int*)ind,
+                (const unsigned*)ks, (const unsigned*)ke, T, (unsigned long long*)mask, mask_words);
+}
+
+GLMKV_API int glmkv_kv_dequant_marked(const void* kv, const int32_t* block_table, int max_pages,
+                                      const int32_t* seq_lens, int nseq, const uint64_t* mask, void* kvd,
+                                      glmkv_stream_t stream) {
+  if (nseq < 0 || max_pages < 0) return GLMKV_ERR_ARG;
+  if (nseq == 0) return GLMKV_OK;
+  if (!kv || !block_table || !seq_lens || !mask || !kvd) return GLMKV_ERR_ARG;
+  if (!aligned(kv, 16) || !aligned(kvd, 16) || !aligned(mask, 8)) return GLMKV_ERR_ALIGN;
+  const DeviceInfo* d = device_info();
+  if (!d) return GLMKV_ERR_DEVICE;
+  return launch(glm_kv_dequant_marked, d->sms * d->dq_ctas, DQ_THREADS, DQ_SMEM, stream, (const u8*)kv, block_table,
+                max_pages, seq_lens, nseq, (const unsigned long long*)mask, (bf16*)kvd);
+}
+
 GLMKV_API int glmkv_topk_stream(int32_t* ind, const uint32_t* ks, const int32_t* klen, int32_t* tlen, int T,
                                 glmkv_stream_t stream) {
   if (T < 0) return GLMKV_ERR_ARG;
@@ -306,10 +342,15 @@ GLMKV_API int glmkv_launch_shape(const char* entry, int T, int* grid, int* block
     *grid = (T + QP_WARPS - 1) / QP_WARPS, *block = QP_THREADS, *smem_bytes = 0;
   } else if (is("glm_topk_stream") || is("glm_topk_slots")) {
     *grid = T, *block = TK_THREADS, *smem_bytes = 0;
-  } else if (is("glm_kv_dequant") || is("glm_idx_gather") || is("glm_mla_prep") || is("glm_mla_prep_fp8")) {
+  } else if (is("glm_mark_rows")) {
     const DeviceInfo* d = device_info();
     if (!d) return GLMKV_ERR_DEVICE;
-    if (is("glm_kv_dequant")) {
+    *grid = std::min(d->sms, std::max(1, (T + MK_RB - 1) / MK_RB)), *block = MK_THREADS, *smem_bytes = MK_SMEM;
+  } else if (is("glm_kv_dequant") || is("glm_kv_dequant_marked") || is("glm_idx_gather") || is("glm_mla_prep") ||
+             is("glm_mla_prep_fp8")) {
+    const DeviceInfo* d = device_info();
+    if (!d) return GLMKV_ERR_DEVICE;
+    if (is("glm_kv_dequant") || is("glm_kv_dequant_marked")) {
       *grid = d->sms * d->dq_ctas, *block = DQ_THREADS, *smem_bytes = (int)DQ_SMEM;
     } else if (is("glm_idx_gather")) {
       *grid = d->sms * d->ga_ctas, *block = GA_THREADS, *smem_bytes = (int)GA_SMEM;
@@ -352,9 +393,9 @@ GLMKV_API const char* glmkv_strerror(int code) {
     case GLMKV_ERR_ARG: return "invalid argument (null pointer or size out of range)";
     case GLMKV_ERR_ALIGN: return "misaligned pointer or row stride";
     case GLMKV_ERR_DEVICE: return "no usable CUDA device";
-    case GLMKV_ERR_LAUNCH: return "kernel launch failed";
+    case GLMKV_ERR_LAUNCH: return "kernel launch (or the launcher's memset) failed";
     default: return "unknown glmkv error";
   }
 }
 
-GLMKV_API int glmkv_abi_version(void) { return 100; }
+GLMKV_API int glmkv_abi_version(void) { return 101; }

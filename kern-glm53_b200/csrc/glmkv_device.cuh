@@ -32,7 +32,7 @@ constexpr unsigned FULL = 0xffffffffu;
 
 // Fault word of the module: bits set by kernels that hit a bounded wait's limit or an invalid page.
 // The host reads and clears it through glmkv_fault_flags().
-enum : unsigned { FAULT_WAIT_TIMEOUT = 1u, FAULT_BAD_PAGE = 2u };
+enum : unsigned { FAULT_WAIT_TIMEOUT = 1u, FAULT_BAD_PAGE = 2u, FAULT_BAD_PICK = 4u };
 
 // ------------------------------------------------------------------------------------------ loads
 

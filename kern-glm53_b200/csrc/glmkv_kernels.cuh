@@ -461,14 +461,18 @@ namespace glmkv {
 
 struct StageMeta {
   unsigned long long row;  // first stream row of the page
+  unsigned long long sel;  // the page's rows to produce (bit i: row i)
   int n;                   // live rows in the page
-  int live;                // 0: past the last page, 1: loaded, 2: skipped (invalid page number)
+  int first;               // the first row staged (the stage holds rows first .. of the page)
+  int live;                // 0: past the last page, 1: loaded, 2: skipped (invalid page number), 3: no row wanted
 };
 
 // A persistent CTA walks the pages b, b + G, b + 2G, ... (G = gridDim.x) of the call's sequences.
 // Thread 0 keeps NSTAGE pages in flight, each one bulk copy (TMA) of the page's bytes into its
 // own shared-memory stage; all threads convert a stage once its mbarrier completes, then thread 0
-// refills it with the CTA's next page. `Op` turns a staged page into its stream rows.
+// refills it with the CTA's next page. `Op` turns a staged page into its stream rows. An Op with
+// SELECTIVE set names the rows of a page it wants (`select`): a page with none is neither read nor
+// written, and only the span from its first to its last wanted row is copied.
 template <int NT, int NSTAGE, class Op>
 __device__ __forceinline__ void page_pipeline(const u8* __restrict__ state, const int* __restrict__ block_table,
                                               int max_pages, const int* __restrict__ seq_lens, int nseq, const Op& op) {
@@ -490,9 +494,23 @@ __device__ __forceinline__ void page_pipeline(const u8* __restrict__ state, cons
     }
     const int j = (int)(g - cur.first);
     const int n = min(PAGE, cur.len - j * PAGE);
-    const int phys = block_table[(size_t)cur.s * max_pages + j];
-    meta[st].row = (unsigned long long)cur.goff + (unsigned long long)j * PAGE;
+    const unsigned long long row0 = (unsigned long long)cur.goff + (unsigned long long)j * PAGE;
+    meta[st].row = row0;
     meta[st].n = n;
+    int first = 0, count = n;
+    if constexpr (Op::SELECTIVE) {
+      const unsigned long long sel = op.select(row0, n);
+      meta[st].sel = sel;
+      if (sel == 0) {  // no row of this page is wanted: nothing to read or write
+        meta[st].live = 3;
+        mbar_arrive(bar);
+        return;
+      }
+      first = __ffsll((long long)sel) - 1;
+      count = 64 - __clzll((long long)sel) - first;
+    }
+    meta[st].first = first;
+    const int phys = block_table[(size_t)cur.s * max_pages + j];
     if (phys < 0) {  // not a page of the state: skip it and flag the call
       meta[st].live = 2;
       atomicOr(&g_fault, FAULT_BAD_PAGE);
@@ -500,9 +518,10 @@ __device__ __forceinline__ void page_pipeline(const u8* __restrict__ state, cons
       return;
     }
     meta[st].live = 1;
-    const uint32_t bytes = Op::load_bytes(n);
+    const uint32_t bytes = Op::load_bytes(count);
     mbar_arrive_expect_tx(bar, bytes);
-    tma_load_1d(smem_u32(smem + (size_t)st * Op::STAGE), state + (size_t)phys * Op::PAGE_BYTES, bytes, bar);
+    tma_load_1d(smem_u32(smem + (size_t)st * Op::STAGE),
+                state + (size_t)phys * Op::PAGE_BYTES + (size_t)first * Op::ROW_BYTES, bytes, bar);
     pending |= 1u << st;
     if ((k / NSTAGE) & 1) pend_parity |= 1u << st;
     else pend_parity &= ~(1u << st);
@@ -535,7 +554,12 @@ __device__ __forceinline__ void page_pipeline(const u8* __restrict__ state, cons
     const StageMeta m = meta[st];
     if (m.live == 0) break;
     if (tid == 0) pending &= ~(1u << st);
-    if (m.live == 1) op.template consume<NT>(smem + (size_t)st * Op::STAGE, m.row, m.n, tid);
+    if (m.live == 1) {
+      if constexpr (Op::SELECTIVE)
+        op.template consume_sel<NT>(smem + (size_t)st * Op::STAGE, m.row, m.first, m.sel, tid);
+      else
+        op.template consume<NT>(smem + (size_t)st * Op::STAGE, m.row, m.n, tid);
+    }
     __syncthreads();
     if (tid == 0) issue(k + NSTAGE);
   }
@@ -549,6 +573,8 @@ constexpr int DQ_STAGES = 4;
 struct DequantOp {
   static constexpr int STAGE = KV8_PAGE;
   static constexpr int PAGE_BYTES = KV8_PAGE;
+  static constexpr int ROW_BYTES = KV8;
+  static constexpr bool SELECTIVE = false;
   bf16* kvd;
   __device__ static uint32_t load_bytes(int n) { return (uint32_t)n * KV8; }
 
@@ -588,6 +614,8 @@ constexpr int GA_STAGES = 8;
 struct GatherOp {
   static constexpr int STAGE = IDX_PAGE;
   static constexpr int PAGE_BYTES = IDX_PAGE;
+  static constexpr int ROW_BYTES = 0;  // the whole page is one copy: keys and scales
+  static constexpr bool SELECTIVE = false;
   u8* kg;
   float* ksf;
   __device__ static uint32_t load_bytes(int) { return IDX_PAGE; }  // keys and scales in one copy
@@ -604,7 +632,329 @@ struct GatherOp {
   }
 };
 
+// ------------------------------------------------------------------------------------------------ marked dequant
+
+// The dequant of only the stream rows a call's picks name. `mask` has a bit for every stream row
+// (word w: rows 64 w .. 64 w + 63, bit i row 64 w + i), set by glm_mark_rows. Rows produce exactly
+// the bytes of DequantOp; rows not marked are not written.
+struct MarkedDequantOp : DequantOp {
+  static constexpr bool SELECTIVE = true;
+  const unsigned long long* mask;
+
+  // the marked rows of the page whose n rows start at stream row row0 (bit i: row i of the page)
+  __device__ __forceinline__ unsigned long long select(unsigned long long row0, int n) const {
+    const unsigned long long w = row0 >> 6;
+    const int b = (int)(row0 & 63);
+    unsigned long long m = __ldg(mask + w) >> b;
+    if (b != 0 && row0 + (unsigned long long)n > (w + 1) * 64) m |= __ldg(mask + w + 1) << (64 - b);
+    return n == 64 ? m : m & ((1ull << n) - 1);
+  }
+
+  // the staged rows first .. 63 - clz(sel) of the page -> their stream rows, marked rows only
+  template <int NT>
+  __device__ __forceinline__ void consume_sel(const u8* __restrict__ stg, unsigned long long row0, int first,
+                                              unsigned long long sel, int tid) const {
+    u8* out = reinterpret_cast<u8*>(kvd) + row0 * KVB;
+    const int count = 64 - __clzll((long long)sel) - first;
+    const int nkv = count << 6;
+#pragma unroll 4
+    for (int i = tid; i < nkv; i += NT) {
+      const int rr = i >> 6, c = i & 63, r = first + rr;
+      if (!((sel >> r) & 1ull)) continue;
+      const u8* src = stg + rr * KV8;
+      const uint2 q = *reinterpret_cast<const uint2*>(src + 8 * c);
+      const float sc = reinterpret_cast<const float*>(src + KVL)[c >> 4];
+      uint4 o;
+      o.x = dequant2((uint16_t)(q.x & 0xffffu), sc);
+      o.y = dequant2((uint16_t)(q.x >> 16), sc);
+      o.z = dequant2((uint16_t)(q.y & 0xffffu), sc);
+      o.w = dequant2((uint16_t)(q.y >> 16), sc);
+      *reinterpret_cast<uint4*>(out + (size_t)r * KVB + 16 * c) = o;
+    }
+    const int npe = count << 3;
+    for (int i = tid; i < npe; i += NT) {
+      const int rr = i >> 3, c = i & 7, r = first + rr;
+      if (!((sel >> r) & 1ull)) continue;
+      *reinterpret_cast<uint4*>(out + (size_t)r * KVB + 2 * KVL + 16 * c) =
+          *reinterpret_cast<const uint4*>(stg + rr * KV8 + KVL + 16 + 16 * c);
+    }
+  }
+};
+
+// ------------------------------------------------------------------------------------------------ mark
+
+constexpr int MK_THREADS = 256;
+constexpr int MK_RB = 4;                           // rows of picks a loop iteration: 8 loads a thread in flight
+constexpr int MK_WORDS = (1 << 20) / 32 + 2;       // shared-memory window: a 2^20-row stream, unaligned
+constexpr int MK_SMEM = MK_WORDS * 4;              // 131,080 B
+
 }  // namespace glmkv
+
+// The stream rows a call's picks name, as a bitmap: bit p % 64 of word p / 64 for every pick p >= 0 of
+// ind [T, 2048] (stream rows, after glm_topk_stream). The launcher clears mask first and sizes the
+// grid so that every SM takes an equal run of rows. A CTA's rows pick inside the stream rows
+// [min ks, max ke) (glm_plan), which it marks in a window of shared memory (2^20 rows at most) with
+// 32-bit atomics (a 64-bit shared-memory OR measured 8x slower), then ORs into mask word by word: one
+// global atomic a word a CTA rather than one a pick. The mask is addressed as 32-bit words, which on
+// this little-endian device is the same bitmap. A pick outside the window (malformed picks) is ORed
+// straight into mask, and one past mask_words * 64 is skipped and flagged (fault bit 4). No counterpart
+// in the reference: it feeds glm_kv_dequant_marked.
+//   grid min(SMs, ceil(T / 4)), block 256, dynamic smem MK_SMEM (131,080 B)
+extern "C" __global__ void __launch_bounds__(glmkv::MK_THREADS)
+    glm_mark_rows(const int* __restrict__ ind, const unsigned* __restrict__ ks, const unsigned* __restrict__ ke,
+                  int T, unsigned long long* __restrict__ mask, int mask_words) {
+  using namespace glmkv;
+  extern __shared__ __align__(16) unsigned win[];
+  __shared__ unsigned s_lo[MK_THREADS / 32], s_hi[MK_THREADS / 32];
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x, l = tid & 31, w = tid >> 5;
+  const int per = (T + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int r0 = min(T, (int)blockIdx.x * per), r1 = min(T, r0 + per);
+  unsigned* const mask32 = reinterpret_cast<unsigned*>(mask);
+  const long long words32 = 2ll * mask_words;
+  // the window: the stream rows these rows' picks can name
+  unsigned lo = 0xffffffffu, hi = 0u;
+  for (int r = r0 + tid; r < r1; r += MK_THREADS) lo = min(lo, ks[r]), hi = max(hi, ke[r]);
+  lo = __reduce_min_sync(FULL, lo);
+  hi = __reduce_max_sync(FULL, hi);
+  if (l == 0) s_lo[w] = lo, s_hi[w] = hi;
+  __syncthreads();
+  lo = 0xffffffffu, hi = 0u;
+#pragma unroll
+  for (int i = 0; i < MK_THREADS / 32; ++i) lo = min(lo, s_lo[i]), hi = max(hi, s_hi[i]);
+  const long long wlo = lo >> 5;
+  const long long whi = min(((long long)hi + 31) >> 5, words32);
+  const int nw = whi > wlo ? (int)(whi - wlo) : 0;
+  const bool windowed = nw <= MK_WORDS;
+  if (windowed)
+    for (int i = tid; i < nw; i += MK_THREADS) win[i] = 0u;
+  __syncthreads();
+  auto put = [&](int p) {
+    if (p < 0) return;
+    const long long wd = p >> 5;
+    const unsigned bit = 1u << (p & 31);
+    if (windowed && wd >= wlo && wd < whi) {
+      atomicOr(&win[wd - wlo], bit);
+    } else if (wd < words32) {
+      atomicOr(mask32 + wd, bit);
+    } else {
+      atomicOr(&g_fault, FAULT_BAD_PICK);
+    }
+  };
+  for (int r = r0; r < r1; r += MK_RB) {
+    int4 v[2 * MK_RB];
+#pragma unroll
+    for (int k = 0; k < MK_RB; ++k) {
+      if (r + k < r1) {
+        const int4* a = reinterpret_cast<const int4*>(ind + (size_t)(r + k) * TOPK);
+        v[2 * k] = ld_stream_v4(a + tid);
+        v[2 * k + 1] = ld_stream_v4(a + MK_THREADS + tid);
+      } else {
+        v[2 * k] = v[2 * k + 1] = make_int4(-1, -1, -1, -1);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 2 * MK_RB; ++k) put(v[k].x), put(v[k].y), put(v[k].z), put(v[k].w);
+  }
+  __syncthreads();
+  if (windowed)
+    for (int i = tid; i < nw; i += MK_THREADS) {
+      const unsigned m = win[i];
+      if (m) atomicOr(mask32 + wlo + i, m);
+    }
+}
+
+namespace glmkv {
+
+constexpr int ML_SEQ = 1024;  // sequences a planned marked lift holds in shared memory (more: cursor walk)
+constexpr int ML_CAP = 1024;  // pages a CTA plans at a time
+constexpr int ML_DENSE = 48;  // a page with this many marked rows is lifted whole
+
+struct MlEntry {
+  unsigned long long row;  // first stream row of the page
+  unsigned long long sel;  // its marked rows
+  int phys;                // its page in the state
+  int n;                   // its live rows
+};
+
+// The marked lift with the CTA's pages planned up front: all threads find, for a batch of the CTA's
+// pages b, b + G, ... at once, each page's sequence (a binary search over the pages of the sequences
+// before it), its marked rows and, when it has any, its page number; the pages with marked rows are
+// compacted, in order, into a list. Thread 0 then streams the listed pages as page_pipeline does, so a
+// page with no marked row costs a mask read and nothing else. A page with ML_DENSE or more marked rows
+// is lifted whole (its other rows get the bytes the full lift writes there): skipping a few rows of a
+// page saves little and costs the page's even run of stores. Needs nseq <= ML_SEQ.
+template <int NT, int NSTAGE>
+__device__ __forceinline__ void marked_pipeline(const u8* __restrict__ state, const int* __restrict__ block_table,
+                                                int max_pages, const int* __restrict__ seq_lens, int nseq,
+                                                const MarkedDequantOp& op) {
+  extern __shared__ __align__(128) u8 smem[];
+  __shared__ __align__(8) unsigned long long full[NSTAGE];
+  __shared__ MlEntry list[ML_CAP];
+  __shared__ int s_len[ML_SEQ], s_pages[ML_SEQ + 1];
+  __shared__ unsigned s_goff[ML_SEQ + 1];
+  __shared__ int s_wsum[NT / 32], s_count;
+  const int tid = threadIdx.x, l = tid & 31, w = tid >> 5;
+  if (tid == 0) {
+#pragma unroll
+    for (int st = 0; st < NSTAGE; ++st) mbar_init(smem_u32(&full[st]), 1);
+    mbar_init_fence();
+  }
+  pdl_trigger();  // a persistent grid: all of its CTAs are resident
+  pdl_wait();
+  // pages and rows of the sequences before each one: a block scan, NT sequences at a time
+  int carry_pages = 0;
+  unsigned carry_rows = 0;
+  for (int base = 0; base < nseq; base += NT) {
+    const int s = base + tid;
+    const int len = s < nseq ? seq_lens[s] : 0;
+    const int pg = (len + PAGE - 1) / PAGE;
+    int ip = pg;
+    unsigned ir = (unsigned)len;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int a = __shfl_up_sync(FULL, ip, o);
+      const unsigned b = __shfl_up_sync(FULL, ir, o);
+      if (l >= o) ip += a, ir += b;
+    }
+    __shared__ unsigned s_wrows[NT / 32];
+    if (l == 31) s_wsum[w] = ip, s_wrows[w] = ir;
+    __syncthreads();
+    int wp = 0;
+    unsigned wr = 0;
+    for (int i = 0; i < w; ++i) wp += s_wsum[i], wr += s_wrows[i];
+    if (s < nseq) {
+      s_len[s] = len;
+      s_pages[s] = carry_pages + wp + ip - pg;  // exclusive prefix
+      s_goff[s] = carry_rows + wr + ir - (unsigned)len;
+    }
+    int tp = 0;
+    unsigned tr = 0;
+    for (int i = 0; i < NT / 32; ++i) tp += s_wsum[i], tr += s_wrows[i];
+    carry_pages += tp, carry_rows += tr;
+    __syncthreads();
+  }
+  if (tid == 0) s_pages[nseq] = carry_pages;
+  __syncthreads();
+  const long long total = carry_pages, G = gridDim.x;
+  const long long mine = total > (long long)blockIdx.x ? (total - 1 - blockIdx.x) / G + 1 : 0;  // this CTA's pages
+
+  long long k = 0;  // stage uses so far (their mbarrier phases)
+  for (long long done = 0; done < mine; done += ML_CAP) {
+    // ---- plan: the next ML_CAP of this CTA's pages, those with marked rows listed in order
+    if (tid == 0) s_count = 0;
+    __syncthreads();
+    for (int b = 0; b < ML_CAP && done + b < mine; b += NT) {
+      const long long kk = done + b + tid;
+      bool want = false;
+      MlEntry e;
+      if (b + tid < ML_CAP && kk < mine) {
+        const int g = (int)(blockIdx.x + kk * G);
+        int lo = 0, hi = nseq - 1;  // the last sequence whose first page is <= g
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (s_pages[mid] <= g) lo = mid;
+          else hi = mid - 1;
+        }
+        const int j = g - s_pages[lo];
+        e.n = min(PAGE, s_len[lo] - j * PAGE);
+        e.row = (unsigned long long)s_goff[lo] + (unsigned long long)j * PAGE;
+        e.sel = op.select(e.row, e.n);
+        if (__popcll(e.sel) >= ML_DENSE) e.sel = e.n == 64 ? ~0ull : (1ull << e.n) - 1;  // lift it whole
+        want = e.sel != 0;
+        if (want) e.phys = block_table[(size_t)lo * max_pages + j];
+      }
+      const unsigned bal = __ballot_sync(FULL, want);
+      if (l == 0) s_wsum[w] = __popc(bal);
+      __syncthreads();
+      int off = 0;
+      for (int i = 0; i < w; ++i) off += s_wsum[i];
+      if (want) list[s_count + off + __popc(bal & ((1u << l) - 1))] = e;
+      __syncthreads();
+      if (tid == 0)
+        for (int i = 0; i < NT / 32; ++i) s_count += s_wsum[i];
+      __syncthreads();
+    }
+    const int count = s_count;
+    // ---- stream the listed pages, NSTAGE in flight
+    unsigned pending = 0, pend_parity = 0;
+    auto issue = [&](int i) {  // list entry i into stage (k + i) % NSTAGE
+      const long long u = k + i;
+      const int st = (int)(u % NSTAGE);
+      const uint32_t bar = smem_u32(&full[st]);
+      if (i >= count) {
+        mbar_arrive(bar);
+        return;
+      }
+      const MlEntry& e = list[i];
+      if (e.phys < 0) {  // not a page of the state: skip it and flag the call
+        atomicOr(&g_fault, FAULT_BAD_PAGE);
+        mbar_arrive(bar);
+        return;
+      }
+      const int first = __ffsll((long long)e.sel) - 1, cnt = 64 - __clzll((long long)e.sel) - first;
+      const uint32_t bytes = (uint32_t)cnt * KV8;
+      mbar_arrive_expect_tx(bar, bytes);
+      tma_load_1d(smem_u32(smem + (size_t)st * KV8_PAGE), state + (size_t)e.phys * KV8_PAGE + (size_t)first * KV8,
+                  bytes, bar);
+      pending |= 1u << st;
+      if ((u / NSTAGE) & 1) pend_parity |= 1u << st;
+      else pend_parity &= ~(1u << st);
+    };
+    if (tid == 0)
+      for (int i = 0; i < NSTAGE; ++i) issue(i);
+    for (int i = 0; i < count; ++i) {
+      const long long u = k + i;
+      const int st = (int)(u % NSTAGE);
+      const bool ok = mbar_wait_bounded(smem_u32(&full[st]), (uint32_t)((u / NSTAGE) & 1), WAIT_LIMIT_NS);
+      if (__syncthreads_or(!ok)) {
+        if (tid == 0) {
+          atomicOr(&g_fault, FAULT_WAIT_TIMEOUT);
+          for (int q = 0; q < NSTAGE; ++q)
+            if (pending & (1u << q)) mbar_wait_bounded(smem_u32(&full[q]), (pend_parity >> q) & 1u, WAIT_LIMIT_NS);
+        }
+        return;
+      }
+      if (tid == 0) pending &= ~(1u << st);
+      const MlEntry e = list[i];
+      if (e.phys >= 0)
+        op.consume_sel<NT>(smem + (size_t)st * KV8_PAGE, e.row, __ffsll((long long)e.sel) - 1, e.sel, tid);
+      __syncthreads();
+      if (tid == 0) issue(i + NSTAGE);
+    }
+    // the NSTAGE stages issued past the list's end completed on plain arrives: consume their phases
+    for (int i = count; i < count + NSTAGE; ++i) {
+      const long long u = k + i;
+      mbar_wait_bounded(smem_u32(&full[(int)(u % NSTAGE)]), (uint32_t)((u / NSTAGE) & 1), WAIT_LIMIT_NS);
+    }
+    k += count + NSTAGE;
+    __syncthreads();
+  }
+}
+
+}  // namespace glmkv
+
+// The stream of glm_kv_dequant restricted to the rows mask marks (glm_mark_rows): a marked row gets
+// exactly the bytes glm_kv_dequant writes there; a page with no marked row is neither read nor
+// written; a page with at least ML_DENSE (48) marked rows is lifted whole, as glm_kv_dequant lifts it;
+// of the other pages only the span from the first to the last marked row is read and only the marked
+// rows are written. (With more than ML_SEQ sequences the lift walks the pages with the cursor and
+// writes marked rows only.) mask must hold ceil(stream / 64) words. No counterpart in the reference,
+// whose lift converts every row (glm_glue.cu:378-414).
+//   persistent: grid = SMs x resident CTAs, block 512, dynamic smem DQ_STAGES * 41984 B
+extern "C" __global__ void __launch_bounds__(glmkv::DQ_THREADS, 1)
+    glm_kv_dequant_marked(const glmkv::u8* __restrict__ kv, const int* __restrict__ block_table, int max_pages,
+                          const int* __restrict__ seq_lens, int nseq, const unsigned long long* __restrict__ mask,
+                          glmkv::bf16* __restrict__ kvd) {
+  glmkv::MarkedDequantOp op;
+  op.kvd = kvd;
+  op.mask = mask;
+  if (nseq <= glmkv::ML_SEQ)
+    glmkv::marked_pipeline<glmkv::DQ_THREADS, glmkv::DQ_STAGES>(kv, block_table, max_pages, seq_lens, nseq, op);
+  else
+    glmkv::page_pipeline<glmkv::DQ_THREADS, glmkv::DQ_STAGES>(kv, block_table, max_pages, seq_lens, nseq, op);
+}
 
 // The indexer keys of every sequence back to back (glm_glue.cu:353-376): page j of sequence s lands
 // at stream rows goff(s) + 64 j, keys in kg [., 128], scales in ksf.

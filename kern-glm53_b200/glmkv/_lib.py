@@ -17,6 +17,8 @@ SIGNATURES = {
     "glmkv_mla_prep_fp8": [P, I, P, P, P, P, P, P, P, P, P, P, P, I, I, P],
     "glmkv_idx_gather": [P, P, I, P, I, P, P, P],
     "glmkv_kv_dequant": [P, P, I, P, I, P, P],
+    "glmkv_mark_rows": [P, P, P, I, P, I, P],
+    "glmkv_kv_dequant_marked": [P, P, I, P, I, P, P, P],
     "glmkv_topk_stream": [P, P, P, P, I, P],
     "glmkv_topk_slots": [P, P, I, P, P, P, I, P],
     "glmkv_q_post": [P, I, P, P, P, P, P, P, I, I, P],

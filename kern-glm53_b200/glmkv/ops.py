@@ -24,6 +24,11 @@ by the op's scalars, exactly in the manifest's parameter order, and enqueues one
     rms_quant        the same without a (nulled, 171)                      glm_add_rms_quant
     head_norm        the same without q, sf (nulled, 156-158)              glm_add_rms_quant
     quant_o          x, ldx, q, sf, sf_rows, K, T         (103-105)        glm_quant
+    mark_rows        ind, ks, ke, T, mask, mask_words: the bitmap of the    glm_mark_rows
+                     stream rows the picks name (no manifest op: feeds
+                     kv_dequant_marked)
+    kv_dequant_marked kv, block_table, max_pages, seq_lens, nseq, mask,  glm_kv_dequant_marked
+                     kvd: the lift of the marked rows only
     mqa_logits_paged iq, idx, n_pages, block_table, max_pages, row_seq,  glm_mqa_logits_paged
                      klen, w, logits, stride, R: the indexer's MQA logits
                      from the cache pages (replaces idx_gather + the MQA
@@ -42,6 +47,7 @@ _DTYPES = {
     "bf16": (torch.bfloat16, torch.int16, torch.uint16),
     "u8": (torch.uint8, torch.int8, torch.float8_e4m3fn),
     "f32": (torch.float32,),
+    "u64": (torch.int64, torch.uint64),
 }
 
 
@@ -104,6 +110,19 @@ def idx_gather(idx, block_table, max_pages, seq_lens, nseq, kg, ksf, stream=None
 def kv_dequant(kv, block_table, max_pages, seq_lens, nseq, kvd, stream=None):
     _lib.call("glmkv_kv_dequant", _ptr(kv, "u8", "kv"), _ptr(block_table, "i32", "block_table"), int(max_pages),
               _ptr(seq_lens, "i32", "seq_lens"), int(nseq), _ptr(kvd, "bf16", "kvd"), _stream(stream))
+
+
+def mark_rows(ind, ks, ke, T, mask, mask_words, stream=None):
+    """The bitmap of the stream rows the picks name (bit p % 64 of word p // 64), cleared first."""
+    _lib.call("glmkv_mark_rows", _ptr(ind, "i32", "ind"), _ptr(ks, "u32", "ks"), _ptr(ke, "u32", "ke"), int(T),
+              _ptr(mask, "u64", "mask"), int(mask_words), _stream(stream))
+
+
+def kv_dequant_marked(kv, block_table, max_pages, seq_lens, nseq, mask, kvd, stream=None):
+    """kv_dequant of the rows `mask` marks only; the other rows of kvd are not written."""
+    _lib.call("glmkv_kv_dequant_marked", _ptr(kv, "u8", "kv"), _ptr(block_table, "i32", "block_table"),
+              int(max_pages), _ptr(seq_lens, "i32", "seq_lens"), int(nseq), _ptr(mask, "u64", "mask"),
+              _ptr(kvd, "bf16", "kvd"), _stream(stream))
 
 
 def topk_stream(ind, ks, klen, tlen, T, stream=None):

@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol(built_lib):
         assert hasattr(lib, name), name
     import glmkv
     assert set(declared()) == set(glmkv._lib.SIGNATURES)
-    assert glmkv.lib().glmkv_abi_version() == 100
+    assert glmkv.lib().glmkv_abi_version() == 101
 
 
 def test_host_side_argument_checks(built_lib):
@@ -83,6 +83,17 @@ def test_host_side_argument_checks(built_lib):
     assert L.glmkv_idx_gather(A, A, -1, A, 1, A, A, None) == _lib.ERR_ARG
     assert L.glmkv_topk_stream(A + 4, A, A, A, 8, None) == _lib.ERR_ALIGN
     assert L.glmkv_topk_slots(A, A, 16, A, A, None, 8, None) == _lib.ERR_ARG
+    assert L.glmkv_mark_rows(A, A, A, -1, A, 16, None) == _lib.ERR_ARG                # T < 0
+    assert L.glmkv_mark_rows(A, A, A, 8, None, 16, None) == _lib.ERR_ARG              # no mask
+    assert L.glmkv_mark_rows(A, A, A, 8, A, 0, None) == _lib.ERR_ARG                  # no mask words
+    assert L.glmkv_mark_rows(A, A, A, 0, A, 0, None) == _lib.OK                       # nothing at all
+    assert L.glmkv_mark_rows(A, A, A, 8, A + 4, 16, None) == _lib.ERR_ALIGN           # mask 8-byte
+    assert L.glmkv_mark_rows(A + 8, A, A, 8, A, 16, None) == _lib.ERR_ALIGN           # ind 16-byte
+    assert L.glmkv_mark_rows(None, A, A, 8, A, 16, None) == _lib.ERR_ARG
+    assert L.glmkv_kv_dequant_marked(A, A, 16, A, 0, A, A, None) == _lib.OK           # nseq = 0
+    assert L.glmkv_kv_dequant_marked(A, A, 16, A, 1, None, A, None) == _lib.ERR_ARG
+    assert L.glmkv_kv_dequant_marked(A, A, 16, A, 1, A + 4, A, None) == _lib.ERR_ALIGN
+    assert L.glmkv_kv_dequant_marked(A + 8, A, 16, A, 1, A, A, None) == _lib.ERR_ALIGN
     with pytest.raises(glmkv.GlmKvError):
         _lib.call("glmkv_topk_stream", A + 4, A, A, A, 8, None)
     assert "misaligned" in glmkv.strerror(_lib.ERR_ALIGN)
