@@ -766,10 +766,7 @@ def main():
     else:  # single-layer workloads: every rank runs layer 0 (an indexer layer) of its own call
         first, last, cuts = 0, 1, [0]
     forwards = stage.forwarded_picks(cuts) if a.workload == "cfg3" else []
-    if forwards:  # before NCCL and the kernels start: p2p kernels on few SMs, and those SMs left to them
-        os.environ.setdefault("NCCL_MAX_P2P_NCHANNELS", str(stage.FORWARD_RESERVED_SMS))
-        if any(rank in (s_, r_) for s_, r_, _ in forwards):
-            os.environ.setdefault("GLMKV_RESERVE_SMS", str(stage.FORWARD_RESERVED_SMS))
+
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     gd.init("nccl", timeout_s=300, device=dev)
@@ -791,7 +788,7 @@ def main():
     torch.cuda.synchronize()
 
     # the picks of an indexer layer before a cut at a shared layer travel to the next stage every call
-    fwd = gd.PicksForwarder(cuts if a.workload == "cfg3" else [0], rank, call.T, dev, ind=ind, tlen=group.tlen)
+    fwd = gd.picks_forwarder(cuts if a.workload == "cfg3" else [0], rank, call.T, dev, ind=ind, tlen=group.tlen)
     if a.impl == "glmkv":
         call_path = lambda hook: group.run_call(meta, inputs, ind, on_op=hook)
     else:
@@ -897,6 +894,7 @@ def main():
         gd.finish()
         return
 
+    forwarder = type(fwd).__name__  # every rank builds the same kind (picks_forwarder decides together)
     if a.workload == "cfg3":
         cost = [sum(stage.layer_bytes(x, call.T, call.ctx) for x in range(f, l)) for f, l in layer_ranges]
         ideal = sum(stage.layer_bytes(x, call.T, call.ctx) for x in range(stage.LAYERS)) / max(cost)
@@ -923,13 +921,16 @@ def main():
             "layers": (stage.LAYERS if a.workload == "cfg3" else world), "stage_cuts": cuts,
             "placement": ("cuts at indexer layers only" if not forwards else
                           "cuts at any layer; the picks of the indexer layer before each cut at a shared layer "
-                          "are forwarded to the next stage every call (NCCL send/recv on a side stream)"),
+                          "are forwarded to the next stage every call, one call ahead (" + (
+                              "copy-engine peer copies through CUDA IPC, ordered by stream memory operations"
+                              if forwarder == "PeerCopyForwarder" else "NCCL send/recv on a side stream") + ")"),
             "forwarded_picks": [{"from_rank": s_, "to_rank": r_, "indexer_layer": l_,
                                  "bytes_per_call": stage.picks_bytes(call.T)} for s_, r_, l_ in forwards],
-            "reserved_sms_on_forwarding_ranks": stage.FORWARD_RESERVED_SMS if forwards else 0,
+            "forwarder": forwarder if forwards else None,
             "parallelism": f"layer groups x{world} (pipeline stages)" + (
-                f", {len(forwards)} forward(s) of the picks a call by NCCL send/recv" if forwards else
-                ", no collective on the data path"),
+                f", {len(forwards)} forward(s) of the picks a call by " + (
+                    "copy-engine peer copies" if forwarder == "PeerCopyForwarder" else "NCCL send/recv")
+                if forwards else ", no collective on the data path"),
             "l2": "no flush: every layer's cache pool and stream exceed the 126 MB L2",
             "storage": "e4m3 codes + f32 scales in, bf16 out; f32 arithmetic",
         },

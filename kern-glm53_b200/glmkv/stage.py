@@ -28,11 +28,9 @@ def layer_bytes(l, T, ctx, kv_dtype="fp8"):
     return traffic.layer(T, ctx, l in FULL, kv_dtype)
 
 
-# SMs a stage that sends or receives forwarded picks leaves to the transfer's kernels (NCCL's p2p
-# kernels stay resident while they wait for the peer), and the slowdown of such a stage's persistent
-# kernels that this costs, as measured on B200 (148 SMs): 4 SMs, about 3%
-FORWARD_RESERVED_SMS = 4
-FORWARD_SLOWDOWN = 0.03
+# The slowdown of a stage that sends or receives forwarded picks by copy-engine peer copies
+# (dist.PeerCopyForwarder), as measured on B200: 0.3% (7.971 against 7.946 ms a call of 39 layers)
+FORWARD_SLOWDOWN = 0.005
 
 
 def cuts(n_groups, T=16384, ctx=1 << 20, kv_dtype="fp8", any_layer=False):

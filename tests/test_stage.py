@@ -34,15 +34,15 @@ def test_any_layer_cuts_and_forwarded_picks():
     total = sum(stage.layer_bytes(l, T, ctx) for l in range(78))
     # where the exchange does not pay for itself the solver keeps to indexer layers (2 and 4 stages: the
     # reference's own cuts at 4)
-    for n, want in ((2, (0, 38)), (4, (0, 18, 38, 58)), (8, (0, 10, 18, 28, 38, 48, 58, 68))):
+    for n, want in ((2, (0, 38)), (4, (0, 18, 38, 58)), (8, (0, 9, 18, 28, 38, 48, 58, 68))):
         c = stage.cuts(n, T=T, ctx=ctx, any_layer=True)
         assert c == want
     c8 = stage.cuts(8, T=T, ctx=ctx, any_layer=True)
     cc = list(c8) + [78]
     cost = [sum(stage.layer_bytes(l, T, ctx) for l in range(cc[i], cc[i + 1])) for i in range(8)]
     assert total / max(cost) > 7.4  # against 6.54 with cuts at indexer layers only
-    # stages starting at shared layers 28, 48, 68 attend with the picks of layers 26, 46, 66
-    assert stage.forwarded_picks(c8) == [(2, 3, 26), (4, 5, 46), (6, 7, 66)]
+    # stages starting at shared layers 9, 28, 48, 68 attend with the picks of layers 6, 26, 46, 66
+    assert stage.forwarded_picks(c8) == [(0, 1, 6), (2, 3, 26), (4, 5, 46), (6, 7, 66)]
     assert stage.forwarded_picks((0, 9, 18)) == [(0, 1, 6)]
     assert stage.forwarded_picks(stage.cuts(4)) == []
     assert [stage.picks_source(l) for l in (0, 2, 3, 5, 6, 9, 77)] == [0, 2, 2, 2, 6, 6, 74]
@@ -145,7 +145,10 @@ def _forward_main(rank, world, port, q, calls):
                 ind[38].copy_(torch.arange(T * 2048, dtype=torch.int32).view(T, 2048) + 1000 * c)
                 tlen.fill_(c + 1)
                 fwd.hook("topk", 38, False)
-            fwd.end_call()
+            if rank == 1 and c % 2 == 0:  # the receive is posted at layer 77 (38's place in stage 0) ...
+                assert fwd.recvs == [(0, 38, 77)]
+                fwd.hook("mla_prep", 77, True)
+            fwd.end_call()  # ... or, on odd calls, when the call ends
         fwd.drain()
         if rank == 1:  # the last call's picks
             a, t = fwd.received(38)
