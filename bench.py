@@ -95,10 +95,17 @@ class ClockSampler:
     def __enter__(self):
         if self.enabled:
             try:
-                cmd = ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "100"]
+                cmd = ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "50"]
                 if self.ids:
                     cmd += ["-i", ",".join(self.ids)]
                 self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                # the sampler is running before the timed region starts (at 8 GPUs that region can be
+                # shorter than nvidia-smi's start-up): wait for its first sample, at most 5 s
+                import select
+                if select.select([self.proc.stdout], [], [], 5.0)[0]:
+                    first = self.proc.stdout.readline()
+                    if first.strip():
+                        self.lines.append(first.strip())
             except OSError:
                 self.proc = None
         return self
@@ -112,7 +119,7 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+            self.lines += [l for l in out.splitlines() if l.strip()]
 
     def summary(self):
         sm, mx, reasons, pw = [], [], set(), []
