@@ -248,7 +248,7 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
     }
     for (int i = 0; i < MQ_KSTAGES; ++i) {
       mbar_init(smem_u32(&k_full[i]), 1);
-      mbar_init(smem_u32(&k_empty[i]), 1 + MQ_EPI_WARPS / 2);  // the MMAs, and the group's warps at the tile's end
+      mbar_init(smem_u32(&k_empty[i]), 1 + MQ_EPI_WARPS / 2);  // the MMAs, and the group's warps once they hold the scales
     }
     mbar_init(smem_u32(&mma_done), 1);
     mbar_init_fence();
@@ -468,10 +468,14 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
           const bool okw = mq_wait(smem_u32(&acc_full[gp]), eph, abort);
           if (__any_sync(FULL, !okw)) return false;  // the warp leaves together: tcgen05.ld is warp-collective
           tc_fence_after();
+          // the key's scale into a register, and the stage back to the producer: the MMAs have read
+          // its keys (they completed before acc_full), so the next copies need not wait for the sums
+          const float scale = reinterpret_cast<const float*>(sgen + (scbuf - sbase) + st * MQ_SCBYTES)[32 * qd + l];
+          __syncwarp();
+          if (l == 0) mbar_arrive(smem_u32(&k_empty[st]));
           const int p = kb * MQ_KEYS + 32 * qd + l;  // this thread's key position
           const int p0 = kb * MQ_KEYS + 32 * qd;
           if (p0 < max(limp0, limp1)) {
-            const float scale = reinterpret_cast<const float*>(sgen + (scbuf - sbase) + st * MQ_SCBYTES)[32 * qd + l];
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
               if (p0 >= (j ? limp1 : limp0)) continue;
@@ -515,10 +519,7 @@ __device__ __forceinline__ void mq_logits(const CUtensorMap* tm_q, const CUtenso
           }
           tc_fence_before();
           __syncwarp();
-          if (l == 0) {  // the stage (its scales) and the accumulator are read
-            mbar_arrive(smem_u32(&k_empty[st]));
-            mbar_arrive(smem_u32(&acc_empty[gp]));
-          }
+          if (l == 0) mbar_arrive(smem_u32(&acc_empty[gp]));  // the accumulator is read
           eph ^= 1;
         }
         return true;
