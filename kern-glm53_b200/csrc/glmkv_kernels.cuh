@@ -683,8 +683,12 @@ struct MarkedDequantOp : DequantOp {
 
 // ------------------------------------------------------------------------------------------------ mark
 
-constexpr int MK_THREADS = 256;
-constexpr int MK_RB = 4;                           // rows of picks a loop iteration: 8 loads a thread in flight
+// 1024 threads: the shared-memory atomics are latency-bound, so the CTA (one an SM: the window takes
+// 128 KB) brings as many warps as it can; 256 threads took twice as long
+constexpr int MK_THREADS = 1024;
+constexpr int MK_RB = 8;                                  // rows of picks a loop iteration
+constexpr int MK_LD = MK_RB * (TOPK / 4) / MK_THREADS;    // 16-byte loads a thread an iteration, all in flight
+static_assert(MK_LD * MK_THREADS == MK_RB * (TOPK / 4), "an iteration's rows split evenly over the threads");
 constexpr int MK_WORDS = (1 << 20) / 32 + 2;       // shared-memory window: a 2^20-row stream, unaligned
 constexpr int MK_SMEM = MK_WORDS * 4;              // 131,080 B
 
@@ -699,7 +703,7 @@ constexpr int MK_SMEM = MK_WORDS * 4;              // 131,080 B
 // this little-endian device is the same bitmap. A pick outside the window (malformed picks) is ORed
 // straight into mask, and one past mask_words * 64 is skipped and flagged (fault bit 4). No counterpart
 // in the reference: it feeds glm_kv_dequant_marked.
-//   grid min(SMs, ceil(T / 4)), block 256, dynamic smem MK_SMEM (131,080 B)
+//   grid min(SMs, ceil(T / 8)), block 1024, dynamic smem MK_SMEM (131,080 B)
 extern "C" __global__ void __launch_bounds__(glmkv::MK_THREADS)
     glm_mark_rows(const int* __restrict__ ind, const unsigned* __restrict__ ks, const unsigned* __restrict__ ke,
                   int T, unsigned long long* __restrict__ mask, int mask_words) {
@@ -743,19 +747,16 @@ extern "C" __global__ void __launch_bounds__(glmkv::MK_THREADS)
     }
   };
   for (int r = r0; r < r1; r += MK_RB) {
-    int4 v[2 * MK_RB];
+    int4 v[MK_LD];
 #pragma unroll
-    for (int k = 0; k < MK_RB; ++k) {
-      if (r + k < r1) {
-        const int4* a = reinterpret_cast<const int4*>(ind + (size_t)(r + k) * TOPK);
-        v[2 * k] = ld_stream_v4(a + tid);
-        v[2 * k + 1] = ld_stream_v4(a + MK_THREADS + tid);
-      } else {
-        v[2 * k] = v[2 * k + 1] = make_int4(-1, -1, -1, -1);
-      }
+    for (int k = 0; k < MK_LD; ++k) {
+      const int f = k * MK_THREADS + tid;  // 16-byte piece f of the MK_RB rows, row-major
+      const int rr = r + f / (TOPK / 4);
+      v[k] = rr < r1 ? ld_stream_v4(reinterpret_cast<const int4*>(ind + (size_t)rr * TOPK) + f % (TOPK / 4))
+                     : make_int4(-1, -1, -1, -1);
     }
 #pragma unroll
-    for (int k = 0; k < 2 * MK_RB; ++k) put(v[k].x), put(v[k].y), put(v[k].z), put(v[k].w);
+    for (int k = 0; k < MK_LD; ++k) put(v[k].x), put(v[k].y), put(v[k].z), put(v[k].w);
   }
   __syncthreads();
   if (windowed)

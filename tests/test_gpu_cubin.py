@@ -231,10 +231,14 @@ def _snippet_shapes():
 
     text = (pathlib.Path(__file__).resolve().parents[1] / "INTEGRATION.md").read_text()
     out = []
-    for m in re.finditer(r'G\.b200\((?:"(glm_\w+)"|prep), \w+, \[(.+?), 1, 1\], \[(\d+), 1, 1\](?:, (\d+))?', text):
+    # G.b200(entry, params, grid, block[, smem]): params a name or a list expression, possibly over lines
+    # (never reaching into the next call); the grid's first element may hold one level of brackets
+    params = r'((?:(?!G\.b200\().)*?)'
+    shape = r'\[((?:[^\[\]]|\[[^\[\]]*\])+?), 1, 1\],\s*\[(\d+), 1, 1\](?:,\s*(\d+))?'
+    for m in re.finditer(r'G\.b200\((?:"(glm_\w+)"|prep),' + params + shape, text, flags=re.S):
         entries = [m.group(1)] if m.group(1) else ["glm_mla_prep_fp8", "glm_mla_prep"]
         for e in entries:
-            out.append((e, m.group(2), int(m.group(3)), int(m.group(4) or 0)))
+            out.append((e, m.group(3), int(m.group(4)), int(m.group(5) or 0)))
     for m in re.finditer(r'launch\("glm_glue_b200", "(glm_\w+)", \[(.+?), 1, 1\], \[(\d+), 1, 1\],\s*(\d+)', text):
         out.append((m.group(1), m.group(2), int(m.group(3)), int(m.group(4))))
     return out
@@ -251,7 +255,8 @@ def test_integration_snippet_matches_the_launch_shapes(cuda):
     T = 16384
     sms = torch.cuda.get_device_properties(cuda).multi_processor_count
     shapes = _snippet_shapes()
-    assert {e for e, *_ in shapes} == set(ENTRIES), sorted({e for e, *_ in shapes})
+    assert {e for e, *_ in shapes} == set(ENTRIES) | {"glm_mark_rows", "glm_kv_dequant_marked"}, \
+        sorted({e for e, *_ in shapes})
 
     def grid_of(expr):
         expr = expr.strip().replace("G.SMS_B200", "SMS").replace("SMS_B200", "SMS")
