@@ -873,6 +873,11 @@ def main():
         e2e_ms = max_over_ranks(max(s2.elapsed_time(e2), 0.0))
         e2e = (e2e_ms, h2d, d2h, max_over_ranks(wall))
 
+    # the last call that moves picks is done: unmap the peers' buffers on every rank before any rank
+    # goes on (ranks other than 0 exit below, which frees the buffers they exported)
+    fwd.close()
+    barrier()
+
     # ---- whole-job numbers
     layer_ranges = list(zip(cuts, cuts[1:] + [stage.LAYERS if a.workload == "cfg3" else 1]))
     total_bytes = 0

@@ -141,6 +141,9 @@ class PicksForwarder:
         self.pending_send = {}
         self._wait_recvs()
 
+    def close(self):
+        """Nothing to unmap: the process group owns the transfers."""
+
     def received(self, src):
         """(ind, tlen) of indexer layer `src` of the last completed receive: while a call runs, the picks
         that call attends with; after `drain`, the last call's."""
@@ -272,6 +275,19 @@ class PeerCopyForwarder:
         main = torch.cuda.current_stream(self.device)
         for src in self.copy_pending:
             main.wait_event(self.copied[src])
+
+    def close(self):
+        """Unmaps the peers' buffers once this rank's copies and stream operations have completed. Every
+        rank closes before any rank frees the buffers it exported (they live as long as the process):
+        callers put a barrier after it, as `picks_forwarder` puts one before the first call."""
+        self.drain()
+        torch.cuda.current_stream(self.device).wait_stream(self.stream)
+        torch.cuda.synchronize(self.device)
+        for base in self._opened.values():
+            self._ck(self.rt.cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle")
+        self._opened.clear()
+        self.peer.clear()
+        self.sends, self.recvs = [], []
 
     def received(self, src):
         """(ind, tlen) of indexer layer `src` that the current (or, between calls, the last) call

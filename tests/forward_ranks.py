@@ -46,6 +46,8 @@ def main():
     fwd.drain()
     torch.cuda.synchronize()
     gd.barrier()
+    fwd.close()  # every rank unmaps its peer's buffers before either frees its own
+    gd.barrier()
     print(f"forward {'ok' if bad == 0 else 'BAD'} rank {rank} {kind} mismatches {bad}", flush=True)
     gd.finish()
     sys.exit(0 if bad == 0 else 1)

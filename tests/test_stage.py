@@ -153,6 +153,7 @@ def _forward_main(rank, world, port, q, calls):
         if rank == 1:  # the last call's picks
             a, t = fwd.received(38)
             got.append((int(a[0]), int(a[-1]), int(t[0])))
+        fwd.close()
         gd.barrier()
         gd.finish()
         q.put((rank, "ok", got, fwd.bytes_per_call))
