@@ -196,7 +196,7 @@ __device__ __forceinline__ void prep_row(const Row& row, const float* __restrict
                                          const float* __restrict__ wik, const float* __restrict__ wib,
                                          const bf16* __restrict__ rope, int p, long long s, u8* __restrict__ kv,
                                          u8* __restrict__ idx, u8* __restrict__ qq, u8* __restrict__ qsf, int sf_rows,
-                                         int r, int l) {
+                                         int r, int l, uint32_t* __restrict__ xw) {
   uint2 qw[16];  // q_a columns kb * 128 + 4l .. + 3
 #pragma unroll
   for (int kb = 0; kb < 16; ++kb) qw[kb] = row.v2(2 * (kb * 128 + 4 * l));
@@ -241,18 +241,29 @@ __device__ __forceinline__ void prep_row(const Row& row, const float* __restrict
   const float bm = __uint_as_float(((l & 1) ? (mw & 0xffff0000u) : (mw << 16)) & 0x7fffffffu);
   unsigned e;
   const float inv = __frcp_rn(ue8m0_div(bm, 1e-10f, &e));  // lane l: block 2 ((l >> 2) & 7) + (l & 1)
+  // Every block's inverse and UE8M0 byte reach the whole warp through its scratch words (one store and
+  // four broadcast loads instead of 16 shuffles): word kb the inverse of block kb, byte 64 + kb its
+  // scale byte, so that word 16 + q is DeepGEMM's packed word q (byte kb & 3 of word kb >> 2).
+  __syncwarp();  // the previous row's reads of the scratch are done
+  if ((l & 2) == 0) {
+    const int blk = 2 * ((l >> 2) & 7) + (l & 1);
+    xw[blk] = __float_as_uint(inv);
+    reinterpret_cast<u8*>(xw + 16)[blk] = (u8)e;
+  }
+  __syncwarp();
   u8* qrow = qq + (size_t)r * QL;
 #pragma unroll
-  for (int kb = 0; kb < 16; ++kb) {
-    const uint32_t iv = __shfl_sync(FULL, __float_as_uint(inv), 4 * (kb >> 1) + (kb & 1));
-    const float2 a = scale_bf16x2(yb[kb][0], iv), b = scale_bf16x2(yb[kb][1], iv);
-    *reinterpret_cast<uint32_t*>(qrow + kb * 128 + 4 * l) = fp8x4(a.x, a.y, b.x, b.y);
-  }
-  // DeepGEMM's packed scales: byte (kb & 3) of word (kb >> 2, r); lane q < 4 writes word q whole.
-  unsigned word = 0;
+  for (int k4 = 0; k4 < 16; k4 += 4) {
+    const uint4 i4 = *reinterpret_cast<const uint4*>(xw + k4);
+    const uint32_t ivs[4] = {i4.x, i4.y, i4.z, i4.w};
 #pragma unroll
-  for (int m = 0; m < 4; ++m) word |= __shfl_sync(FULL, e, 8 * (l & 3) + 4 * (m >> 1) + (m & 1)) << (8 * m);
-  if (l < 4) *reinterpret_cast<unsigned*>(qsf + ((size_t)l * sf_rows + r) * 4) = word;
+    for (int j = 0; j < 4; ++j) {
+      const int kb = k4 + j;
+      const float2 a = scale_bf16x2(yb[kb][0], ivs[j]), b = scale_bf16x2(yb[kb][1], ivs[j]);
+      *reinterpret_cast<uint32_t*>(qrow + kb * 128 + 4 * l) = fp8x4(a.x, a.y, b.x, b.y);
+    }
+  }
+  if (l < 4) *reinterpret_cast<unsigned*>(qsf + ((size_t)l * sf_rows + r) * 4) = xw[16 + l];
 
   if (s < 0) return;  // no cache slot: nothing more to write (glm_glue.cu:231-232)
 
@@ -279,14 +290,22 @@ __device__ __forceinline__ void prep_row(const Row& row, const float* __restrict
     const float tm = __uint_as_float(((l & 1) ? (m & 0xffff0000u) : (m << 16)) & 0x7fffffffu);
     const float sc = __fdiv_rn(tm, 448.f);
     const float tinv = sc > 0.f ? __frcp_rn(sc) : 0.f;
+    // each tile's inverse and scale through the scratch as well: words 20 + t and 24 + t
+    if ((l & 14) == 0) {
+      const int t = 2 * (l >> 4) + (l & 1);
+      xw[20 + t] = __float_as_uint(tinv);
+      xw[24 + t] = __float_as_uint(sc);
+    }
+    __syncwarp();
+    const uint4 t4 = *reinterpret_cast<const uint4*>(xw + 20);
+    const float tiv[4] = {__uint_as_float(t4.x), __uint_as_float(t4.y), __uint_as_float(t4.z), __uint_as_float(t4.w)};
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
-      const float iv = __shfl_sync(FULL, tinv, 16 * (w >> 2) + ((w >> 1) & 1));
+      const float iv = tiv[w >> 1];  // virtual warp w is in tile w / 2
       const float2 q = mul2(unpack2(kn[w]), make_float2(iv, iv));
       *reinterpret_cast<uint16_t*>(dst + 2 * (32 * w + l)) = fp8x2(q.x, q.y);
     }
-    const float sct = __shfl_sync(FULL, sc, 16 * ((l & 3) >> 1) + (l & 1));
-    if (l < 4) reinterpret_cast<float*>(dst + KVL)[l] = sct;
+    if (l < 4) reinterpret_cast<uint32_t*>(dst + KVL)[l] = xw[24 + l];
   } else {
 #pragma unroll
     for (int w = 0; w < 8; ++w) *reinterpret_cast<uint32_t*>(dst + 4 * (32 * w + l)) = kn[w];
@@ -355,6 +374,7 @@ __device__ __forceinline__ void prep_rows(const bf16* __restrict__ x, int lda, c
                                           int sf_rows, int T) {
   extern __shared__ __align__(128) u8 smem[];
   __shared__ __align__(8) unsigned long long bar[PREP_WARPS][PREP_BUFS];
+  __shared__ __align__(16) uint32_t xws[PREP_WARPS][32];  // each warp's broadcast scratch (prep_row)
   float* wq = reinterpret_cast<float*>(smem);
   float* wkv = wq + QL;
   float* wik = wkv + KVL;
@@ -407,7 +427,7 @@ __device__ __forceinline__ void prep_rows(const bf16* __restrict__ x, int lda, c
   if (!bulk) {
     for (; r < T; r += stride)
       prep_row<FP8>(GlobalRow{reinterpret_cast<const u8*>(x + (size_t)r * lda)}, wq, wkv, wik, wib, rope, pos[r],
-                    slot[r], kv, idx, qq, qsf, sf_rows, r, l);
+                    slot[r], kv, idx, qq, qsf, sf_rows, r, l, xws[warp]);
     return;
   }
   int p = pos[r];
@@ -428,7 +448,8 @@ __device__ __forceinline__ void prep_rows(const bf16* __restrict__ x, int lda, c
       }
       return;
     }
-    prep_row<FP8>(SmemRow{buf + b * PREP_ROW}, wq, wkv, wik, wib, rope, p, s, kv, idx, qq, qsf, sf_rows, r, l);
+    prep_row<FP8>(SmemRow{buf + b * PREP_ROW}, wq, wkv, wik, wib, rope, p, s, kv, idx, qq, qsf, sf_rows, r, l,
+                  xws[warp]);
     __syncwarp();
     p = pn, s = sn;
   }
