@@ -6,8 +6,10 @@ A step is one packed prefill call (cfg3: 16 sequences, 16,384 fresh rows, prefix
 256K}, at most 2^20 stream tokens) through the cache path of all 78 layers: per stage its row plan,
 then per layer the append (fp8 latent row + q quant, and the indexer key on indexer layers), on
 indexer layers the key gather and the top-k row plan, and the paged dequant of every sequence's
-prefix + chunk. With N GPUs the 78 layers are cut into N stages at indexer layers, one stage a GPU,
-with no collective on the data path (pipeline parallelism, as the reference deploys it).
+prefix + chunk. With N GPUs the 78 layers are cut into N stages, one stage a GPU (pipeline
+parallelism, as the reference deploys it): at indexer layers, or also at shared layers where that
+balances better, with the picks of the indexer layer before such a cut copied to the next stage once a
+call (copy-engine peer copies; the one transfer on the data path).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl glmkv|reference] [--workload cfg3|cfg1|cfg2]
     torchrun --nproc-per-node N bench.py --gpus N ...
@@ -625,11 +627,34 @@ def marked_block(torch, impl, group, meta, call, dev, peak, passes=2):
         return s_.elapsed_time(e_) / n * 1e3
 
     out = {"note": "mask from one indexer layer's picks after the row plan; lift timed back to back over the "
-                   "stage's layers; the full lift (glm_kv_dequant) timed the same way beside it"}
+                   "stage's layers; the full lift (glm_kv_dequant) timed the same way beside it; row_plan_us and "
+                   "row_plan_and_mark_fused_us: glm_topk_stream alone and glm_topk_stream_mark, each launch on a "
+                   "fresh copy of the sequence-relative picks"}
     lift_all = lambda: [glmkv.kv_dequant(group.kv[l], meta.block_table, mp, meta.seq_lens, call.nseq, group.kvd)
                         for l in group.layers]
     full_us = timed(lift_all, passes) / len(group.layers)
+    fresh = torch.empty_like(dists["uniform"])
+    tl = torch.empty_like(group.tlen)
+    m2 = torch.empty_like(mask)
+    s1, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed_fresh(fn, picks, n=6):
+        """fn rewrites its picks in place: each launch gets a fresh copy of `picks` before its own events."""
+        spans = []
+        for i in range(n + 1):
+            fresh.copy_(picks)
+            s1.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            if i:
+                spans.append(s1.elapsed_time(e1) * 1e3)
+        return sum(spans) / len(spans)
+
     for name, picks in dists.items():
+        plan_us = timed_fresh(lambda: glmkv.topk_stream(fresh, group.ks, group.klen, tl, T), picks)
+        fused_us = timed_fresh(lambda: glmkv.topk_stream_mark(fresh, group.ks, group.klen, tl, T, group.ke, m2, words),
+                               picks)
         ind = picks.clone()
         glmkv.topk_stream(ind, group.ks, group.klen, group.tlen, T)
         mark = lambda: glmkv.mark_rows(ind, group.ks, group.ke, T, mask, words)
@@ -664,7 +689,12 @@ def marked_block(torch, impl, group, meta, call, dev, peak, passes=2):
                      "lift_frac": round(lift_bytes / lift_us / 1e3 / peak, 4),
                      "full_lift_us": round(full_us, 2),
                      "full_lift_bytes": traffic.kv_dequant(ctx),
-                     "speedup_vs_full_lift_incl_mark_every_4_layers": round(full_us / (lift_us + mark_us / 4), 3)}
+                     "speedup_vs_full_lift_incl_mark_every_4_layers": round(full_us / (lift_us + mark_us / 4), 3),
+                     # the row plan and the mark in one pass (glm_topk_stream_mark) against the row plan
+                     # alone: what marking adds when fused
+                     "row_plan_us": round(plan_us, 2), "row_plan_and_mark_fused_us": round(fused_us, 2),
+                     "speedup_vs_full_lift_incl_fused_mark_every_4_layers":
+                         round(full_us / (lift_us + max(fused_us - plan_us, 0.0) / 4), 3)}
         del ind
     return out
 

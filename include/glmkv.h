@@ -99,6 +99,16 @@ int glmkv_kv_dequant(const void* kv, const int32_t* block_table, int max_pages, 
 int glmkv_mark_rows(const int32_t* ind, const uint32_t* ks, const uint32_t* ke, int T, uint64_t* mask, int mask_words,
                     glmkv_stream_t stream);
 
+/* glmkv_topk_stream and glmkv_mark_rows in one pass over the picks: ind [T, 2048] i32 arrives
+ * sequence-relative and leaves as stream rows (in place, the bytes glmkv_topk_stream writes), tlen as
+ * glmkv_topk_stream writes it, and mask as glmkv_mark_rows builds it from those stream rows. The first
+ * five parameters are glmkv_topk_stream's, the rest glmkv_mark_rows'. Clears mask first, as
+ * glmkv_mark_rows does. Needs ind 16-byte aligned, mask 8. No counterpart in the reference: it
+ * replaces op `topk_stream` (kern-glm53 scripts/gen.py:130-132; source/glm_glue.cu:416-428) on an
+ * indexer layer whose picks the row-selective lift uses. */
+int glmkv_topk_stream_mark(int32_t* ind, const uint32_t* ks, const int32_t* klen, int32_t* tlen, int T,
+                           const uint32_t* ke, uint64_t* mask, int mask_words, glmkv_stream_t stream);
+
 /* glmkv_kv_dequant restricted to the rows mask marks (glmkv_mark_rows): every marked stream row gets
  * exactly the bytes glmkv_kv_dequant writes there. A page with no marked row is neither read nor
  * written. A page with 48 or more marked rows is lifted whole (its other rows get the bytes
@@ -165,8 +175,8 @@ int glmkv_mqa_logits_paged(const void* iq, const void* idx, int n_pages, const i
 /* The launch shape (grid x, block x, dynamic shared memory bytes) libglmkv uses for the kernel
  * `entry` ("glm_plan", "glm_mla_prep", "glm_mla_prep_fp8", "glm_idx_gather", "glm_kv_dequant",
  * "glm_topk_stream", "glm_topk_slots", "glm_q_post", "glm_add_rms_quant", "glm_mqa_logits_paged",
- * "glm_mark_rows", "glm_kv_dequant_marked") on
- * the current device for a call of T fresh rows: what a kern
+ * "glm_mark_rows", "glm_topk_stream_mark", "glm_kv_dequant_marked") on the current device for a
+ * call of T fresh rows: what a kern
  * manifest's `impl.launches` entry for the cubin must use. The persistent page kernels depend on the
  * device's SM count only. No counterpart in the reference, whose shapes are fixed in its manifest
  * generator (kern-glm53 scripts/gen.py:95-135, 172-177). */

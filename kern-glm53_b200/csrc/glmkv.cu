@@ -64,6 +64,8 @@ const DeviceInfo* device_info() {
                                     (int)DQ_SMEM) == cudaSuccess;
     ok = ok && cudaFuncSetAttribute(glm_mark_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, MK_SMEM) ==
                    cudaSuccess;
+    ok = ok && cudaFuncSetAttribute(glm_topk_stream_mark, cudaFuncAttributeMaxDynamicSharedMemorySize, MK_SMEM) ==
+                   cudaSuccess;
     ok = ok && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.ga_ctas, glm_idx_gather, GA_THREADS, GA_SMEM) ==
                    cudaSuccess;
     for (auto k : {glm_mla_prep, glm_mla_prep_fp8})
@@ -201,8 +203,11 @@ GLMKV_API int glmkv_kv_dequant(const void* kv, const int32_t* block_table, int m
                 max_pages, seq_lens, nseq, (bf16*)kvd);
 }
 
-GLMKV_API int glmkv_mark_rows(const int32_t* ind, const uint32_t* ks, const uint32_t* ke, int T, uint64_t* mask,
-                              int mask_words, glmkv_stream_t stream) {
+// The checks and the clearing memset of the two marking launchers; GLMKV_OK with *go set when a
+// launch of `grid` CTAs follows.
+static int mark_prologue(const void* ind, const void* ks, const void* ke, int T, uint64_t* mask, int mask_words,
+                         glmkv_stream_t stream, bool* go, int* grid) {
+  *go = false;
   if (T < 0 || mask_words < 0) return GLMKV_ERR_ARG;
   if (mask_words == 0) return T == 0 ? GLMKV_OK : GLMKV_ERR_ARG;
   if (!mask) return GLMKV_ERR_ARG;
@@ -215,9 +220,30 @@ GLMKV_API int glmkv_mark_rows(const int32_t* ind, const uint32_t* ks, const uint
     cudaGetLastError();
     return GLMKV_ERR_LAUNCH;
   }
-  if (T == 0) return GLMKV_OK;
-  return launch(glm_mark_rows, std::min(d->sms, (T + MK_RB - 1) / MK_RB), MK_THREADS, MK_SMEM, stream, (const int*)ind,
-                (const unsigned*)ks, (const unsigned*)ke, T, (unsigned long long*)mask, mask_words);
+  *go = T > 0;
+  *grid = std::min(d->sms, (T + MK_RB - 1) / MK_RB);
+  return GLMKV_OK;
+}
+
+GLMKV_API int glmkv_mark_rows(const int32_t* ind, const uint32_t* ks, const uint32_t* ke, int T, uint64_t* mask,
+                              int mask_words, glmkv_stream_t stream) {
+  bool go;
+  int grid = 0;
+  const int rc = mark_prologue(ind, ks, ke, T, mask, mask_words, stream, &go, &grid);
+  if (rc != GLMKV_OK || !go) return rc;
+  return launch(glm_mark_rows, grid, MK_THREADS, MK_SMEM, stream, (const int*)ind, (const unsigned*)ks,
+                (const unsigned*)ke, T, (unsigned long long*)mask, mask_words);
+}
+
+GLMKV_API int glmkv_topk_stream_mark(int32_t* ind, const uint32_t* ks, const int32_t* klen, int32_t* tlen, int T,
+                                     const uint32_t* ke, uint64_t* mask, int mask_words, glmkv_stream_t stream) {
+  if (T > 0 && (!klen || !tlen)) return GLMKV_ERR_ARG;
+  bool go;
+  int grid = 0;
+  const int rc = mark_prologue(ind, ks, ke, T, mask, mask_words, stream, &go, &grid);
+  if (rc != GLMKV_OK || !go) return rc;
+  return launch(glm_topk_stream_mark, grid, MK_THREADS, MK_SMEM, stream, (int*)ind, (const unsigned*)ks,
+                (const int*)klen, (int*)tlen, T, (const unsigned*)ke, (unsigned long long*)mask, mask_words);
 }
 
 GLMKV_API int glmkv_kv_dequant_marked(const void* kv, const int32_t* block_table, int max_pages,
@@ -342,7 +368,7 @@ GLMKV_API int glmkv_launch_shape(const char* entry, int T, int* grid, int* block
     *grid = (T + QP_WARPS - 1) / QP_WARPS, *block = QP_THREADS, *smem_bytes = 0;
   } else if (is("glm_topk_stream") || is("glm_topk_slots")) {
     *grid = T, *block = TK_THREADS, *smem_bytes = 0;
-  } else if (is("glm_mark_rows")) {
+  } else if (is("glm_mark_rows") || is("glm_topk_stream_mark")) {
     const DeviceInfo* d = device_info();
     if (!d) return GLMKV_ERR_DEVICE;
     *grid = std::min(d->sms, std::max(1, (T + MK_RB - 1) / MK_RB)), *block = MK_THREADS, *smem_bytes = MK_SMEM;
@@ -398,4 +424,4 @@ GLMKV_API const char* glmkv_strerror(int code) {
   }
 }
 
-GLMKV_API int glmkv_abi_version(void) { return 101; }
+GLMKV_API int glmkv_abi_version(void) { return 102; }

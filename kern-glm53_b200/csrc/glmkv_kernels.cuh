@@ -713,22 +713,23 @@ static_assert(MK_LD * MK_THREADS == MK_RB * (TOPK / 4), "an iteration's rows spl
 constexpr int MK_WORDS = (1 << 20) / 32 + 2;       // shared-memory window: a 2^20-row stream, unaligned
 constexpr int MK_SMEM = MK_WORDS * 4;              // 131,080 B
 
-}  // namespace glmkv
+// a sequence-relative pick as a row of the dequantized stream (glm_glue.cu:421-425): -1 stays -1
+__device__ __forceinline__ int stream_row(int k, unsigned base) { return k < 0 ? -1 : (int)(base + (unsigned)k); }
 
-// The stream rows a call's picks name, as a bitmap: bit p % 64 of word p / 64 for every pick p >= 0 of
-// ind [T, 2048] (stream rows, after glm_topk_stream). The launcher clears mask first and sizes the
-// grid so that every SM takes an equal run of rows. A CTA's rows pick inside the stream rows
-// [min ks, max ke) (glm_plan), which it marks in a window of shared memory (2^20 rows at most) with
-// 32-bit atomics (a 64-bit shared-memory OR measured 8x slower), then ORs into mask word by word: one
-// global atomic a word a CTA rather than one a pick. The mask is addressed as 32-bit words, which on
-// this little-endian device is the same bitmap. A pick outside the window (malformed picks) is ORed
-// straight into mask, and one past mask_words * 64 is skipped and flagged (fault bit 4). No counterpart
-// in the reference: it feeds glm_kv_dequant_marked.
-//   grid min(SMs, ceil(T / 8)), block 1024, dynamic smem MK_SMEM (131,080 B)
-extern "C" __global__ void __launch_bounds__(glmkv::MK_THREADS)
-    glm_mark_rows(const int* __restrict__ ind, const unsigned* __restrict__ ks, const unsigned* __restrict__ ke,
-                  int T, unsigned long long* __restrict__ mask, int mask_words) {
-  using namespace glmkv;
+// The body of glm_mark_rows and glm_topk_stream_mark: a CTA takes an equal run of rows [r0, r1), whose
+// picks lie inside the stream rows [min ks, max ke) (glm_plan). It marks them in a window of shared
+// memory (2^20 rows at most) with 32-bit atomics (a 64-bit shared-memory OR measured 8x slower), then
+// ORs the window into mask word by word: one global atomic a word a CTA rather than one a pick. The
+// mask is addressed as 32-bit words, which on this little-endian device is the same bitmap. A pick
+// outside the window (malformed picks) is ORed straight into mask, and one past mask_words * 64 is
+// skipped and flagged (fault bit 4). With REMAP the picks arrive sequence-relative (-1 past a short
+// row's keys) and are first rewritten in place as the stream rows glm_topk_stream writes, with tlen
+// as it writes it (glm_glue.cu:416-428), so that the row plan and the mark read the picks once.
+template <bool REMAP>
+__device__ __forceinline__ void mark_rows(int* __restrict__ ind, const unsigned* __restrict__ ks,
+                                          const int* __restrict__ klen, int* __restrict__ tlen,
+                                          const unsigned* __restrict__ ke, int T, unsigned long long* __restrict__ mask,
+                                          int mask_words) {
   extern __shared__ __align__(16) unsigned win[];
   __shared__ unsigned s_lo[MK_THREADS / 32], s_hi[MK_THREADS / 32];
   pdl_trigger();
@@ -773,18 +774,61 @@ extern "C" __global__ void __launch_bounds__(glmkv::MK_THREADS)
     for (int k = 0; k < MK_LD; ++k) {
       const int f = k * MK_THREADS + tid;  // 16-byte piece f of the MK_RB rows, row-major
       const int rr = r + f / (TOPK / 4);
-      v[k] = rr < r1 ? ld_stream_v4(reinterpret_cast<const int4*>(ind + (size_t)rr * TOPK) + f % (TOPK / 4))
-                     : make_int4(-1, -1, -1, -1);
+      const int4* src = reinterpret_cast<const int4*>(ind + (size_t)rr * TOPK) + f % (TOPK / 4);
+      if constexpr (REMAP)  // read, then rewritten below: a plain load, not the read-only path
+        v[k] = rr < r1 ? *src : make_int4(-1, -1, -1, -1);
+      else
+        v[k] = rr < r1 ? ld_stream_v4(src) : make_int4(-1, -1, -1, -1);
+    }
+    if constexpr (REMAP) {
+#pragma unroll
+      for (int k = 0; k < MK_LD; ++k) {
+        const int f = k * MK_THREADS + tid;
+        const int rr = r + f / (TOPK / 4);
+        if (rr < r1) {
+          const unsigned base = ks[rr];
+          v[k] = make_int4(stream_row(v[k].x, base), stream_row(v[k].y, base), stream_row(v[k].z, base),
+                           stream_row(v[k].w, base));
+          reinterpret_cast<int4*>(ind + (size_t)rr * TOPK)[f % (TOPK / 4)] = v[k];
+        }
+      }
     }
 #pragma unroll
     for (int k = 0; k < MK_LD; ++k) put(v[k].x), put(v[k].y), put(v[k].z), put(v[k].w);
   }
+  if constexpr (REMAP)
+    for (int r = r0 + tid; r < r1; r += MK_THREADS) tlen[r] = min(klen[r], TOPK);
   __syncthreads();
   if (windowed)
     for (int i = tid; i < nw; i += MK_THREADS) {
       const unsigned m = win[i];
       if (m) atomicOr(mask32 + wlo + i, m);
     }
+}
+
+}  // namespace glmkv
+
+// The stream rows a call's picks name, as a bitmap: bit p % 64 of word p / 64 for every pick p >= 0 of
+// ind [T, 2048] (stream rows, after glm_topk_stream). The launcher clears mask first and sizes the
+// grid so that every SM takes an equal run of rows (mark_rows above). No counterpart in the
+// reference: it feeds glm_kv_dequant_marked.
+//   grid min(SMs, ceil(T / 8)), block 1024, dynamic smem MK_SMEM (131,080 B)
+extern "C" __global__ void __launch_bounds__(glmkv::MK_THREADS)
+    glm_mark_rows(const int* __restrict__ ind, const unsigned* __restrict__ ks, const unsigned* __restrict__ ke,
+                  int T, unsigned long long* __restrict__ mask, int mask_words) {
+  glmkv::mark_rows<false>(const_cast<int*>(ind), ks, nullptr, nullptr, ke, T, mask, mask_words);
+}
+
+// glm_topk_stream and glm_mark_rows in one pass over the picks: ind [T, 2048] sequence-relative in,
+// stream rows out (in place), tlen = min(klen, 2048), and the bitmap of the stream rows named. Its
+// first five parameters are glm_topk_stream's; ke, mask and mask_words are glm_mark_rows'. No
+// counterpart in the reference.
+//   grid min(SMs, ceil(T / 8)), block 1024, dynamic smem MK_SMEM (131,080 B)
+extern "C" __global__ void __launch_bounds__(glmkv::MK_THREADS)
+    glm_topk_stream_mark(int* __restrict__ ind, const unsigned* __restrict__ ks, const int* __restrict__ klen,
+                         int* __restrict__ tlen, int T, const unsigned* __restrict__ ke,
+                         unsigned long long* __restrict__ mask, int mask_words) {
+  glmkv::mark_rows<true>(ind, ks, klen, tlen, ke, T, mask, mask_words);
 }
 
 namespace glmkv {
@@ -1016,7 +1060,6 @@ extern "C" __global__ void __launch_bounds__(glmkv::DQ_THREADS, 1)
 namespace glmkv {
 constexpr int TK_THREADS = 256;  // a row of 2048 indices: two int4 a thread
 
-__device__ __forceinline__ int stream_row(int k, unsigned base) { return k < 0 ? -1 : (int)(base + (unsigned)k); }
 __device__ __forceinline__ int slot_of(int k, const int* __restrict__ bt) {
   return k < 0 ? -1 : bt[k >> 6] * PAGE + (k & (PAGE - 1));
 }

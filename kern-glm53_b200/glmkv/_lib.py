@@ -18,6 +18,7 @@ SIGNATURES = {
     "glmkv_idx_gather": [P, P, I, P, I, P, P, P],
     "glmkv_kv_dequant": [P, P, I, P, I, P, P],
     "glmkv_mark_rows": [P, P, P, I, P, I, P],
+    "glmkv_topk_stream_mark": [P, P, P, P, I, P, P, I, P],
     "glmkv_kv_dequant_marked": [P, P, I, P, I, P, P, P],
     "glmkv_topk_stream": [P, P, P, P, I, P],
     "glmkv_topk_slots": [P, P, I, P, P, P, I, P],

@@ -27,6 +27,9 @@ by the op's scalars, exactly in the manifest's parameter order, and enqueues one
     mark_rows        ind, ks, ke, T, mask, mask_words: the bitmap of the    glm_mark_rows
                      stream rows the picks name (no manifest op: feeds
                      kv_dequant_marked)
+    topk_stream_mark ind, ks, klen, tlen, T, ke, mask, mask_words:   glm_topk_stream_mark
+                     topk_stream and mark_rows in one pass (replaces
+                     topk_stream where the marked lift is used)
     kv_dequant_marked kv, block_table, max_pages, seq_lens, nseq, mask,  glm_kv_dequant_marked
                      kvd: the lift of the marked rows only
     mqa_logits_paged iq, idx, n_pages, block_table, max_pages, row_seq,  glm_mqa_logits_paged
@@ -116,6 +119,14 @@ def mark_rows(ind, ks, ke, T, mask, mask_words, stream=None):
     """The bitmap of the stream rows the picks name (bit p % 64 of word p // 64), cleared first."""
     _lib.call("glmkv_mark_rows", _ptr(ind, "i32", "ind"), _ptr(ks, "u32", "ks"), _ptr(ke, "u32", "ke"), int(T),
               _ptr(mask, "u64", "mask"), int(mask_words), _stream(stream))
+
+
+def topk_stream_mark(ind, ks, klen, tlen, T, ke, mask, mask_words, stream=None):
+    """topk_stream (ind sequence-relative in, stream rows out, in place; tlen) and mark_rows of the
+    result, in one pass over the picks."""
+    _lib.call("glmkv_topk_stream_mark", _ptr(ind, "i32", "ind"), _ptr(ks, "u32", "ks"), _ptr(klen, "i32", "klen"),
+              _ptr(tlen, "i32", "tlen"), int(T), _ptr(ke, "u32", "ke"), _ptr(mask, "u64", "mask"), int(mask_words),
+              _stream(stream))
 
 
 def kv_dequant_marked(kv, block_table, max_pages, seq_lens, nseq, mask, kvd, stream=None):

@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol(built_lib):
         assert hasattr(lib, name), name
     import glmkv
     assert set(declared()) == set(glmkv._lib.SIGNATURES)
-    assert glmkv.lib().glmkv_abi_version() == 101
+    assert glmkv.lib().glmkv_abi_version() == 102
 
 
 def test_host_side_argument_checks(built_lib):
@@ -90,6 +90,16 @@ def test_host_side_argument_checks(built_lib):
     assert L.glmkv_mark_rows(A, A, A, 8, A + 4, 16, None) == _lib.ERR_ALIGN           # mask 8-byte
     assert L.glmkv_mark_rows(A + 8, A, A, 8, A, 16, None) == _lib.ERR_ALIGN           # ind 16-byte
     assert L.glmkv_mark_rows(None, A, A, 8, A, 16, None) == _lib.ERR_ARG
+    F = L.glmkv_topk_stream_mark  # ind, ks, klen, tlen, T, ke, mask, mask_words, stream
+    assert F(A, A, A, A, -1, A, A, 16, None) == _lib.ERR_ARG                           # T < 0
+    assert F(A, A, A, A, 8, A, None, 16, None) == _lib.ERR_ARG                         # no mask
+    assert F(A, A, A, A, 8, A, A, 0, None) == _lib.ERR_ARG                             # no mask words
+    assert F(A, A, A, A, 0, A, A, 0, None) == _lib.OK                                  # nothing at all
+    assert F(A, A, None, A, 8, A, A, 16, None) == _lib.ERR_ARG                         # no klen
+    assert F(A, A, A, None, 8, A, A, 16, None) == _lib.ERR_ARG                         # no tlen
+    assert F(A, A, A, A, 8, None, A, 16, None) == _lib.ERR_ARG                         # no ke
+    assert F(A, A, A, A, 8, A, A + 4, 16, None) == _lib.ERR_ALIGN                      # mask 8-byte
+    assert F(A + 8, A, A, A, 8, A, A, 16, None) == _lib.ERR_ALIGN                      # ind 16-byte
     assert L.glmkv_kv_dequant_marked(A, A, 16, A, 0, A, A, None) == _lib.OK           # nseq = 0
     assert L.glmkv_kv_dequant_marked(A, A, 16, A, 1, None, A, None) == _lib.ERR_ARG
     assert L.glmkv_kv_dequant_marked(A, A, 16, A, 1, A + 4, A, None) == _lib.ERR_ALIGN

@@ -255,7 +255,7 @@ def test_integration_snippet_matches_the_launch_shapes(cuda):
     T = 16384
     sms = torch.cuda.get_device_properties(cuda).multi_processor_count
     shapes = _snippet_shapes()
-    assert {e for e, *_ in shapes} == set(ENTRIES) | {"glm_mark_rows", "glm_kv_dequant_marked"}, \
+    assert {e for e, *_ in shapes} == set(ENTRIES) | {"glm_mark_rows", "glm_kv_dequant_marked", "glm_topk_stream_mark"}, \
         sorted({e for e, *_ in shapes})
 
     def grid_of(expr):

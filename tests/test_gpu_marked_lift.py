@@ -2,6 +2,8 @@
 glm_kv_dequant_marked (the lift of those rows only), against the reference's own full lift
 (kern-glm53 source/glm_glue.cu:378-414, compiled unmodified): every marked row bit-exact, every
 other row of the stream untouched, and the bitmap equal to the set of picks computed on the host.
+glm_topk_stream_mark (the row plan and the mark in one pass) must give the reference's
+glm_topk_stream output (glm_glue.cu:416-428) and glm_mark_rows' bitmap, bit for bit.
 FlashMLA reads only the picked rows (kern-glm53 README.md:30-31, scripts/gen.py:399-400), so these
 are the rows its attention sees."""
 import numpy as np
@@ -52,6 +54,7 @@ def _run(cuda, ref, call, seed, ind_rel, nan_codes=False):
     assert glmkv.fault_flags() == 0
     picks = ind.cpu().numpy()
     assert np.array_equal(picks, _stream_picks(call, ind_rel)), "the row plan"
+    _check_fused(cuda, ref, d, T, ind_rel, ind, mask, words)
     want = _host_mask(picks, words)
     got_bits = np.unpackbits(mask.cpu().numpy().view(np.uint8), bitorder="little").astype(bool)
     assert np.array_equal(got_bits, want), "the mark bitmap"
@@ -63,6 +66,26 @@ def _run(cuda, ref, call, seed, ind_rel, nan_codes=False):
     assert torch.equal(o[wr], f[wr]), "lifted rows vs the reference's lift"
     assert torch.all(o[~wr] == SENTINEL), "rows that are not to be lifted were written"
     return float(marked.mean())
+
+
+def _check_fused(cuda, ref, d, T, ind_rel, ind_stream, mask, words):
+    """glm_topk_stream_mark on the same sequence-relative picks: the reference's row plan (ind, tlen)
+    and glm_mark_rows' bitmap, bit for bit."""
+    import glmkv
+
+    want_ind = torch.from_numpy(np.ascontiguousarray(ind_rel)).to(cuda)
+    want_tlen = torch.full((T,), -7, dtype=torch.int32, device=cuda)
+    ref.topk_stream(want_ind.data_ptr(), d["ks"].data_ptr(), d["klen"].data_ptr(), want_tlen.data_ptr(), T)
+    got_ind = torch.from_numpy(np.ascontiguousarray(ind_rel)).to(cuda)
+    got_tlen = torch.full((T,), -7, dtype=torch.int32, device=cuda)
+    got_mask = torch.empty(words, dtype=torch.int64, device=cuda).fill_(-1)  # the launcher clears it
+    glmkv.topk_stream_mark(got_ind, d["ks"], d["klen"], got_tlen, T, d["ke"], got_mask, words)
+    torch.cuda.synchronize()
+    assert glmkv.fault_flags() == 0
+    assert torch.equal(got_ind, want_ind), "fused row plan vs the reference's glm_topk_stream"
+    assert torch.equal(got_ind, ind_stream), "fused row plan vs glm_topk_stream"
+    assert torch.equal(got_tlen, want_tlen), "fused tlen vs the reference's"
+    assert torch.equal(got_mask, mask), "fused bitmap vs glm_mark_rows"
 
 
 def _written_rows(call, marked, dense=48, planned_seqs=1024):
@@ -148,6 +171,16 @@ def test_mark_flags_picks_past_the_bitmap(cuda):
     assert glmkv.fault_flags(clear=True) == 4
     m = mask.cpu().numpy().view(np.uint64)
     assert list(m) == [(1 << 0) | (1 << 63), 1, 0, 1 << 63]
+    # the fused op on the same picks as sequence-relative ones (ks = 0): the same bitmap and flag
+    tlen = torch.zeros(T, dtype=torch.int32, device=cuda)
+    klen = torch.full((T,), 300, dtype=torch.int32, device=cuda)
+    mask2 = torch.zeros(words, dtype=torch.int64, device=cuda)
+    ind2 = ind.clone()
+    glmkv.topk_stream_mark(ind2, ks, klen, tlen, T, ke, mask2, words)
+    torch.cuda.synchronize()
+    assert glmkv.fault_flags(clear=True) == 4
+    assert torch.equal(mask2, mask) and torch.equal(ind2, ind)
+    assert torch.all(tlen == 300)
 
 
 def test_marked_lift_more_sequences_than_planned(cuda, ref):
