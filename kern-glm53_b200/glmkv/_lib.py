@@ -79,7 +79,8 @@ def launch_shape(entry, T=0):
 
 
 def fault_flags(clear=True):
-    """The module's device fault bits on the current device (1: a wait timed out, 2: a bad page)."""
+    """The module's device fault bits on the current device (1: a wait timed out, 2: a bad page, 4: a pick
+    past the mark bitmap)."""
     v = ctypes.c_uint32(0)
     call("glmkv_fault_flags", ctypes.byref(v), int(bool(clear)))
     return v.value
