@@ -14,10 +14,10 @@
  * ik_b), load-time constants read before that wait: they must not be written by the kernel launched
  * just before the append.
  *
- * The persistent kernels (append, gather, dequant, add_rms_quant, MQA logits) size their grids for
- * every SM of the device, less GLMKV_RESERVE_SMS when the environment sets it (read once per device, at
- * the first launch): SMs left to other kernels that stay resident beside the path, such as a transfer
- * that waits for its peer.
+ * The persistent kernels (append, gather, dequant and its marked form, the marks, add_rms_quant, MQA
+ * logits) size their grids for every SM of the device, less GLMKV_RESERVE_SMS when the environment
+ * sets it (read once per device, at the first launch): SMs left to other kernels that stay resident
+ * beside the path, such as a transfer that waits for its peer.
  *
  * Return value: GLMKV_OK, or a GLMKV_ERR_* code when an argument is invalid (nothing is launched) or
  * the launch failed. Device-side conditions (an invalid page number in a block table, a bounded wait
