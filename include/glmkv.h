@@ -12,7 +12,8 @@
  * start while the kernel before it on the stream drains, and waits for it before it reads anything
  * that kernel can have written. The one exception is the append's norm weights (g_q, g_kv, ik_w,
  * ik_b), load-time constants read before that wait: they must not be written by the kernel launched
- * just before the append.
+ * just before the append. (The append also prefetches its first rows of x into L2 before the wait; a
+ * prefetch reads no value into the kernel, so it needs no such condition.)
  *
  * The persistent kernels (append, gather, dequant and its marked form, the marks, add_rms_quant, MQA
  * logits) size their grids for every SM of the device, less GLMKV_RESERVE_SMS when the environment

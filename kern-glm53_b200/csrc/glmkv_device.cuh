@@ -241,6 +241,11 @@ __device__ __forceinline__ void tma_load_1d(uint32_t dst, const void* src, uint3
                "l"(src), "r"(bytes), "r"(bar)
                : "memory");
 }
+// A bulk prefetch of `bytes` (a multiple of 16, the address 16-byte aligned) of THIS GPU's global memory
+// into L2. A hint: it moves no data into the program's view and changes no value.
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 
 // Programmatic dependent launch. A kernel launched with programmatic stream serialization may start
 // while the kernel before it on the stream is finishing; it must not touch global memory before

@@ -386,6 +386,14 @@ __device__ __forceinline__ void prep_rows(const bf16* __restrict__ x, int lda, c
     mbar_init_fence();
   }
   pdl_trigger();  // a persistent grid: all of its CTAs are resident
+  // The warp's first two rows into L2 before the wait: a prefetch is a hint that changes no value (L2 is
+  // where the previous kernel's writes land), and it overlaps that kernel's drain (0.6% of the step).
+  if (l == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (lda & 7) == 0) {
+    const uint32_t nb = idx != nullptr ? PREP_ROW : 2 * (QL + MLA);
+    const int r0 = blockIdx.x * PREP_WARPS + warp, st = gridDim.x * PREP_WARPS;
+    if (r0 < T) prefetch_l2(x + (size_t)r0 * lda, nb);
+    if (r0 + st < T) prefetch_l2(x + (size_t)(r0 + st) * lda, nb);
+  }
 
   // The norm weights as f32, every load in flight at once (g_q and the indexer weights 8-byte aligned,
   // g_kv 4-byte aligned; the launcher checks). They are load-time weights that no kernel of the path
