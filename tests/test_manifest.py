@@ -131,3 +131,23 @@ def test_nulled_arguments_are_optional_in_our_launchers():
             assert "NULL" in block, name
             for i in spec["nulled"]:
                 assert names[i] in block, (name, names[i])
+
+
+def test_integration_snippets_are_all_parsed():
+    """Every `G.b200(...)` launch of INTEGRATION.md's manifest snippets is one that the GPU test of the
+    launch shapes (tests/test_gpu_cubin.py) parses, and names a kernel the cubin exports: a snippet the
+    parser skipped would escape that check."""
+    from test_gpu_cubin import _snippet_shapes
+
+    text = (ROOT / "INTEGRATION.md").read_text()
+    calls = re.findall(r'G\.b200\((?:"(glm_\w+)"|(prep))', text)
+    want = []
+    for entry, prep in calls:
+        want += ["glm_mla_prep_fp8", "glm_mla_prep"] if prep else [entry]
+    shapes = _snippet_shapes()
+    got = [e for e, *_ in shapes if e != "glm_mqa_logits_paged"]  # that one is a `launch(...)`, not G.b200
+    assert got == want
+    assert any(e == "glm_mqa_logits_paged" for e, *_ in shapes)
+    src = KERNELS.read_text() + (ROOT / "kern-glm53_b200" / "csrc" / "glmkv_mqa.cuh").read_text()
+    for e, *_ in shapes:
+        assert re.search(r'extern "C" __global__ void(?:\s+__launch_bounds__\([^)]*\))?\s+' + e + r"\(", src), e
